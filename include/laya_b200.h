@@ -1,0 +1,133 @@
+/*
+ * laya_b200.h -- C ABI of the B200 (sm_100a) backend for the laya encoder
+ * forward pass.
+ *
+ * The boundary is the reference's coarse engine seam (zerodegress/laya-rust):
+ *   trait Engine { fn info(&self) -> EngineInfo; fn forward(&mut self, &Req) -> Out; }
+ * (src/engine.rs:79-82) with Req (src/engine.rs:1-10) and Out
+ * (src/engine.rs:12-17).  A Rust `CudaEngine` shim replacing
+ * src/backend/cuda/mod.rs binds the functions below; INTEGRATION.md shows it.
+ *
+ * Conventions
+ *   - Every function returns LAYA_OK (0) or a nonzero status; the message of
+ *     the calling thread's last failure is laya_last_error().  Nothing aborts
+ *     the process (the reference panics; the shim maps status -> panic!).
+ *   - Plain pointers and sizes only.  Host arrays are borrowed for the call.
+ *   - One engine per GPU; an engine is used by one thread at a time
+ *     (the reference's Engine takes &mut self and is not Sync).
+ */
+#ifndef LAYA_B200_H
+#define LAYA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  LAYA_OK = 0,
+  LAYA_E_INVALID = 1,        /* malformed request or argument            */
+  LAYA_E_LOAD = 2,           /* GGUF / weight validation failure         */
+  LAYA_E_CUDA = 3,           /* CUDA runtime error                       */
+  LAYA_E_DEVICE_TIMEOUT = 4, /* a bounded device-side wait expired       */
+  LAYA_E_STATE = 5           /* call not valid in the engine's state     */
+};
+
+typedef struct laya_engine laya_engine;
+typedef struct laya_plan laya_plan;
+
+/* engine::Req (src/engine.rs:1-10).  ids/att are [n*l], mpos/mmask [n*k],
+ * qtype [n]; att is 1 for real tokens and 0 for padding. */
+typedef struct {
+  int64_t n, l, k;
+  const int64_t *ids;
+  const int64_t *att;
+  const int64_t *mpos;
+  const int64_t *mmask;
+  const int64_t *qtype;
+} laya_req;
+
+/* Message of the calling thread's most recent failure ("" if none). */
+const char *laya_last_error(void);
+
+/* Opens an engine on `device` and loads every weight from a GGUF v3 file,
+ * validating metadata and shapes as Tensors::open does
+ * (src/weights.rs:138-222, 233-245, 353-395).  Replaces CudaEngine::load
+ * (src/backend/cuda/mod.rs:82-148). */
+int laya_open(int device, const char *gguf_path, laya_engine **out);
+
+/* Opens an engine with no weights, for a host that keeps its own GGUF loader
+ * (the reference's gguf.rs / weights.rs): upload each of the 207 tensors with
+ * laya_upload_weight_*, then laya_finalize. */
+int laya_open_empty(int device, laya_engine **out);
+
+/* Uploads one tensor named as in src/arch.rs, in STORED layout (the GGUF /
+ * PyTorch [out, in] layout, dims as Tensors::stored_dims reports them,
+ * src/weights.rs:261-268) -- not the transposed graph layout. */
+int laya_upload_weight_f16(laya_engine *e, const char *name, const uint16_t *data,
+                           const int64_t *stored_dims, int ndims);
+int laya_upload_weight_f32(laya_engine *e, const char *name, const float *data,
+                           const int64_t *stored_dims, int ndims);
+/* Checks that all 207 tensors are present. */
+int laya_finalize(laya_engine *e);
+
+/* Engine::forward (src/engine.rs:81; CudaEngine::forward,
+ * src/backend/cuda/mod.rs:466-812).  logits: n*k floats, act: n*2 floats,
+ * host memory, written before return.  Requests must have att in prefix form
+ * (ones then zeros in every row, at least one real token), qtype < 3,
+ * 0 <= mpos < l, and mpos inside the real tokens where mmask != 0 -- the
+ * layout build_batch produces (src/main.rs:470-500). */
+int laya_forward(laya_engine *e, const laya_req *req, float *logits, float *act);
+
+/* TapSink (src/ops.rs:1-3): like laya_forward, and also calls fn with the
+ * stages enc.{i}, final, head.{i}, logits, act.  Row stages are [n*l, 1024]
+ * f32 in padded layout with zeros in padded rows.  Diagnostic path (slow). */
+typedef void (*laya_tap_fn)(void *user, const char *stage, const float *data, size_t count);
+int laya_forward_tapped(laya_engine *e, const laya_req *req, float *logits, float *act,
+                        laya_tap_fn fn, void *user);
+
+/* EngineInfo (src/engine.rs:71-77) as a JSON object in buf. */
+int laya_info(laya_engine *e, char *buf, size_t len);
+void laya_close(laya_engine *e);
+
+/* ---- device-resident execution (no counterpart in the reference) -------------
+ * A plan is a validated request uploaded once to device memory; running it
+ * enqueues the forward on the engine's stream without host copies, so the
+ * kernels can be timed with inputs resident in HBM. */
+int laya_plan_create(laya_engine *e, const laya_req *req, laya_plan **out);
+int laya_plan_run(laya_engine *e, laya_plan *p);
+/* Synchronizes the stream, checks the device error word, copies outputs. */
+int laya_plan_outputs(laya_engine *e, laya_plan *p, float *logits, float *act);
+/* Captures the plan's launches into a CUDA graph; later runs replay it. */
+int laya_plan_capture(laya_engine *e, laya_plan *p);
+/* real_tokens: sum of real lengths; launches: kernels one run enqueues;
+ * upload_bytes: bytes laya_forward copies host -> device for this request. */
+int laya_plan_stats(laya_plan *p, int64_t *real_tokens, int64_t *launches, int64_t *upload_bytes);
+/* Runs the plan `steps` times with a CUDA event recorded after every launch
+ * and sums device time per launch kind into ms[LAYA_PROF_KINDS] and the
+ * launch counts into launches[LAYA_PROF_KINDS].  Kinds: 0 GEMM QKV (encoder),
+ * 1 GEMM attention-out, 2 GEMM FFN-in + GeGLU, 3 GEMM FFN-out, 4 GEMM head
+ * layers and scorer, 5 attention, 6 row norms, 7 tail. */
+#define LAYA_PROF_KINDS 8
+int laya_plan_profile(laya_engine *e, laya_plan *p, int steps, double *ms, int64_t *launches);
+void laya_plan_destroy(laya_plan *p);
+/* The cudaStream_t the engine launches on. */
+void *laya_stream(laya_engine *e);
+
+/* ---- kernel self-tests (no counterpart in the reference) --------------------
+ * Host in, host out; used by the GPU tests to check single kernels. */
+/* out[M,N] (f32) = A[M,K] . W[N,K]^T with A, W f16; N % 256 == 0, K % 64 == 0. */
+int laya_selftest_gemm(int device, const uint16_t *a, const uint16_t *w, float *out, int m,
+                       int n, int k);
+/* Ragged attention on qkv [R,3072] f16 (q,k pre-scaled) for sequences packed
+ * back to back with lengths lens[n]; window < 0 for global.  out [R,1024] f32. */
+int laya_selftest_attention(int device, const uint16_t *qkv, const int32_t *lens, int n,
+                            int window, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAYA_B200_H */

@@ -1,0 +1,1134 @@
+// Host engine behind the C ABI (include/laya_b200.h).
+//
+// Replaces laya-rust's CudaEngine (src/backend/cuda/mod.rs): weight residency,
+// buffer arena, per-request upload and the launch sequence of the forward.
+// The graph it runs is graph.rs:86-186; the weight roles and stored shapes are
+// arch.rs:263-322 and weights.rs:353-395; metadata checks weights.rs:138-222.
+//
+// Differences from the reference, by design:
+//   * weights stay f16 as stored ([out, in], K-major), no widening and no host
+//     transposes (the reference widens to f32 and transposes 120 tensors);
+//   * the forward runs on the real tokens only: each row's att prefix is
+//     compacted into one token-major buffer (cu_seqlens layout), the padded
+//     positions are never computed (their outputs never reach logits/act);
+//   * no mask tensor: attention takes (length, window) predicates.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/laya_b200.h"
+#include "gguf_reader.h"
+#include "kernels.h"
+
+namespace laya {
+
+// ---- constants (arch.rs:1-15) -------------------------------------------------------
+constexpr int H = 1024, NH = 16, HD = 64, NLAYER = 28, INTER = 2624, NVOCAB = 50368;
+constexpr float SCALE = 0.3535533845424652f, EPS = 1e-5f;
+constexpr int WINDOW = 64, HEAD_LAYERS = 2, HEAD_INTER = 4096, ACT_HIDDEN = 256, ACT_INPUT = H + 4;
+constexpr int QTYPES = 3, GLOBAL_EVERY = 3;
+constexpr int INTER_PAD = 2688;  // 21 tiles of 128 gate columns (2624 rounded up)
+
+namespace {
+
+thread_local std::string g_err;
+
+struct Error : std::runtime_error {
+  int code;
+  Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+std::string fmt(const char* f, ...) __attribute__((format(printf, 1, 2)));
+std::string fmt(const char* f, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(buf, sizeof buf, f, ap);
+  va_end(ap);
+  return buf;
+}
+
+void ck(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Error(LAYA_E_CUDA, fmt("%s: %s", what, cudaGetErrorString(e)));
+}
+
+template <class F>
+int guard(F&& f) {
+  try {
+    f();
+    g_err.clear();
+    return LAYA_OK;
+  } catch (const Error& e) {
+    g_err = e.what();
+    return e.code;
+  } catch (const std::bad_alloc&) {
+    g_err = "out of host memory";
+    return LAYA_E_INVALID;
+  } catch (const std::exception& e) {
+    g_err = e.what();
+    return LAYA_E_LOAD;
+  }
+}
+
+uint16_t f2h_bits(float f) {
+  __half h = __float2half_rn(f);
+  uint16_t b;
+  memcpy(&b, &h, 2);
+  return b;
+}
+
+float h2f_bits(uint16_t b) {
+  __half_raw r;
+  r.x = b;
+  return __half2float(__half(r));
+}
+
+// ---- weight roles ---------------------------------------------------------------------
+enum class Kind { Linear, Embed, F32Vec, F32Mat, Rope, ActW1 };
+
+struct Role {
+  Kind kind;
+  std::vector<int64_t> shape;  // stored shape (weights.rs:353-395)
+};
+
+std::string attn_norm(int i) {
+  return i == 0 ? "encoder.embeddings.norm.weight" : fmt("encoder.layers.%d.attn_norm.weight", i);
+}
+
+std::map<std::string, Role> build_roles() {
+  std::map<std::string, Role> r;
+  r["encoder.embeddings.tok_embeddings.weight"] = {Kind::Embed, {NVOCAB, H}};
+  r["type_emb.weight"] = {Kind::Embed, {QTYPES, H}};
+  r["encoder.final_norm.weight"] = {Kind::F32Vec, {H}};
+  r["rope.freq_full"] = {Kind::Rope, {HD / 2}};
+  r["rope.freq_sliding"] = {Kind::Rope, {HD / 2}};
+  r["scorer.0.weight"] = {Kind::F32Vec, {H}};
+  r["scorer.0.bias"] = {Kind::F32Vec, {H}};
+  r["scorer.1.weight"] = {Kind::Linear, {H, H}};
+  r["scorer.1.bias"] = {Kind::F32Vec, {H}};
+  r["scorer.3.weight"] = {Kind::F32Mat, {1, H}};
+  r["scorer.3.bias"] = {Kind::F32Vec, {1}};
+  r["act_head.0.weight"] = {Kind::ActW1, {ACT_HIDDEN, ACT_INPUT}};
+  r["act_head.0.bias"] = {Kind::F32Vec, {ACT_HIDDEN}};
+  r["act_head.2.weight"] = {Kind::F32Mat, {2, ACT_HIDDEN}};
+  r["act_head.2.bias"] = {Kind::F32Vec, {2}};
+  for (int i = 0; i < NLAYER; ++i) {
+    r[attn_norm(i)] = {Kind::F32Vec, {H}};
+    r[fmt("encoder.layers.%d.mlp_norm.weight", i)] = {Kind::F32Vec, {H}};
+    r[fmt("encoder.layers.%d.attn.Wqkv.weight", i)] = {Kind::Linear, {3 * H, H}};
+    r[fmt("encoder.layers.%d.attn.Wo.weight", i)] = {Kind::Linear, {H, H}};
+    r[fmt("encoder.layers.%d.mlp.Wi.weight", i)] = {Kind::Linear, {2 * INTER, H}};
+    r[fmt("encoder.layers.%d.mlp.Wo.weight", i)] = {Kind::Linear, {H, INTER}};
+  }
+  for (int i = 0; i < HEAD_LAYERS; ++i) {
+    auto n = [&](const char* s) { return fmt("head.layers.%d.%s", i, s); };
+    r[n("norm1.weight")] = {Kind::F32Vec, {H}};
+    r[n("norm1.bias")] = {Kind::F32Vec, {H}};
+    r[n("norm2.weight")] = {Kind::F32Vec, {H}};
+    r[n("norm2.bias")] = {Kind::F32Vec, {H}};
+    r[n("self_attn.in_proj_weight")] = {Kind::Linear, {3 * H, H}};
+    r[n("self_attn.in_proj_bias")] = {Kind::F32Vec, {3 * H}};
+    r[n("self_attn.out_proj.weight")] = {Kind::Linear, {H, H}};
+    r[n("self_attn.out_proj.bias")] = {Kind::F32Vec, {H}};
+    r[n("linear1.weight")] = {Kind::Linear, {HEAD_INTER, H}};
+    r[n("linear1.bias")] = {Kind::F32Vec, {HEAD_INTER}};
+    r[n("linear2.weight")] = {Kind::Linear, {H, HEAD_INTER}};
+    r[n("linear2.bias")] = {Kind::F32Vec, {H}};
+  }
+  return r;
+}
+
+const std::map<std::string, Role>& roles() {
+  static const std::map<std::string, Role> r = build_roles();
+  return r;
+}
+
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
+  ~DevBuf() { release(); }
+  void release() {
+    if (p) cudaFree(p);
+    p = nullptr;
+    bytes = 0;
+  }
+  void alloc(size_t b, const char* what) {
+    release();
+    ck(cudaMalloc(&p, b), what);
+    bytes = b;
+  }
+  template <class T>
+  T* as() const {
+    return static_cast<T*>(p);
+  }
+};
+
+struct Weight {
+  DevBuf buf;
+  CUtensorMap tmap;  // Linear weights only
+  std::vector<float> host;  // small tensors the host also needs (rope, scorer bias)
+  bool present = false;
+};
+
+// Host-side plan of one request: validated and compacted (real tokens only).
+struct HostPlan {
+  int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
+  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row;
+  std::vector<int2> blocks;
+  std::vector<uint8_t> rowtype;
+  std::vector<int8_t> mmask;
+};
+
+// Offsets of each array inside one packed device buffer.
+struct PlanLayout {
+  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, blocks, rowtype, mmask, total;
+};
+
+size_t up256(size_t x) { return (x + 255) / 256 * 256; }
+
+PlanLayout layout_for(const HostPlan& p) {
+  PlanLayout L{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o += up256(bytes ? bytes : 1);
+    return at;
+  };
+  L.tok = take(sizeof(int) * p.R);
+  L.pos = take(sizeof(int) * p.R);
+  L.seq_start = take(sizeof(int) * p.n);
+  L.seq_len = take(sizeof(int) * p.n);
+  L.cls_row = take(sizeof(int) * p.n);
+  L.mk_row = take(sizeof(int) * p.n * p.k);
+  L.blocks = take(sizeof(int2) * p.nblocks);
+  L.rowtype = take(p.R);
+  L.mmask = take((size_t)p.n * p.k);
+  L.total = o;
+  return L;
+}
+
+void pack(const HostPlan& p, const PlanLayout& L, uint8_t* dst) {
+  memcpy(dst + L.tok, p.tok.data(), sizeof(int) * p.R);
+  memcpy(dst + L.pos, p.pos.data(), sizeof(int) * p.R);
+  memcpy(dst + L.seq_start, p.seq_start.data(), sizeof(int) * p.n);
+  memcpy(dst + L.seq_len, p.seq_len.data(), sizeof(int) * p.n);
+  memcpy(dst + L.cls_row, p.cls_row.data(), sizeof(int) * p.n);
+  memcpy(dst + L.mk_row, p.mk_row.data(), sizeof(int) * p.n * p.k);
+  memcpy(dst + L.blocks, p.blocks.data(), sizeof(int2) * p.nblocks);
+  memcpy(dst + L.rowtype, p.rowtype.data(), p.R);
+  memcpy(dst + L.mmask, p.mmask.data(), (size_t)p.n * p.k);
+}
+
+// Validates a Req and compacts its real tokens.  The reference asserts
+// n, l, k > 0 (graph.rs:93) and indexes ids / mpos / qtype unchecked
+// (cpu/mod.rs:145-153, 372-398) -- out-of-range values panic there and are
+// rejected here.
+HostPlan make_plan(const laya_req* q) {
+  if (!q) throw Error(LAYA_E_INVALID, "null request");
+  if (q->n <= 0 || q->l <= 0 || q->k <= 0)
+    throw Error(LAYA_E_INVALID, fmt("request needs n, l, k > 0 (got %lld, %lld, %lld)", (long long)q->n,
+                                    (long long)q->l, (long long)q->k));
+  if (!q->ids || !q->att || !q->mpos || !q->mmask || !q->qtype) throw Error(LAYA_E_INVALID, "null request array");
+  if (q->n > (1 << 20) || q->l > (1 << 16) || q->k > 4096 || q->n * q->l > (1 << 24))
+    throw Error(LAYA_E_INVALID, "request too large");
+  HostPlan p;
+  p.n = (int)q->n;
+  p.l = (int)q->l;
+  p.k = (int)q->k;
+  p.seq_start.resize(p.n);
+  p.seq_len.resize(p.n);
+  int R = 0;
+  for (int b = 0; b < p.n; ++b) {
+    const int64_t* att = q->att + (size_t)b * p.l;
+    int r = 0;
+    while (r < p.l && att[r] != 0) ++r;
+    for (int t = r; t < p.l; ++t)
+      if (att[t] != 0)
+        throw Error(LAYA_E_INVALID,
+                    fmt("row %d: att is not a prefix of ones (real token at %d after padding at %d)", b, t, r));
+    if (r == 0) throw Error(LAYA_E_INVALID, fmt("row %d has no real tokens", b));
+    const int64_t qt = q->qtype[b];
+    if (qt < 0 || qt >= QTYPES) throw Error(LAYA_E_INVALID, fmt("row %d: qtype %lld out of range", b, (long long)qt));
+    p.seq_start[b] = R;
+    p.seq_len[b] = r;
+    R += r;
+  }
+  p.R = R;
+  p.tok.resize(R);
+  p.pos.resize(R);
+  p.rowtype.resize(R);
+  for (int b = 0; b < p.n; ++b) {
+    const int64_t* ids = q->ids + (size_t)b * p.l;
+    for (int t = 0; t < p.l; ++t)
+      if (ids[t] < 0 || ids[t] >= NVOCAB)
+        throw Error(LAYA_E_INVALID, fmt("row %d: token id %lld at %d out of range", b, (long long)ids[t], t));
+    for (int t = 0; t < p.seq_len[b]; ++t) {
+      p.tok[p.seq_start[b] + t] = (int)ids[t];
+      p.pos[p.seq_start[b] + t] = t;
+      p.rowtype[p.seq_start[b] + t] = (uint8_t)q->qtype[b];
+    }
+    for (int q0 = 0; q0 < p.seq_len[b]; q0 += kAttnQRows) p.blocks.push_back(make_int2(b, q0));
+  }
+  p.nblocks = (int)p.blocks.size();
+  p.cls_row.resize(p.n);
+  p.mk_row.resize((size_t)p.n * p.k);
+  p.mmask.resize((size_t)p.n * p.k);
+  for (int b = 0; b < p.n; ++b) {
+    p.cls_row[b] = p.seq_start[b];
+    for (int j = 0; j < p.k; ++j) {
+      const size_t i = (size_t)b * p.k + j;
+      const int64_t mp = q->mpos[i];
+      const bool on = q->mmask[i] != 0;
+      if (mp < 0 || mp >= p.l)
+        throw Error(LAYA_E_INVALID, fmt("marker %d of row %d: position %lld outside [0, %d)", j, b, (long long)mp, p.l));
+      if (on && mp >= p.seq_len[b])
+        throw Error(LAYA_E_INVALID, fmt("marker %d of row %d at %lld points at padding (real length %d)", j, b,
+                                        (long long)mp, p.seq_len[b]));
+      p.mmask[i] = on ? 1 : 0;
+      // masked markers read the sequence's first row: their logit is
+      // replaced by -10000 regardless of the score (cpu/mod.rs:409)
+      p.mk_row[i] = p.seq_start[b] + (on ? (int)mp : 0);
+    }
+  }
+  return p;
+}
+
+}  // namespace
+
+struct DevicePlan {
+  HostPlan host;
+  PlanLayout lay;
+  DevBuf own;              // the plan's own device copy (laya_plan_create)
+  uint8_t* base = nullptr; // where the packed arrays live (own, or the engine's buffer)
+  cudaGraphExec_t graph = nullptr;
+  uint64_t graph_arena_gen = 0;
+  int64_t launches = 0;
+  ~DevicePlan() {
+    if (graph) cudaGraphExecDestroy(graph);
+  }
+  template <class T>
+  const T* at(size_t off) const {
+    return reinterpret_cast<const T*>(base + off);
+  }
+};
+
+struct Engine {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string device_name;
+  std::map<std::string, Weight> w;
+  float temperature[3] = {1, 1, 1};
+  std::string temperature_by_options = "{}";
+  int file_type = 1;
+  bool finalized = false;
+
+  // rope tables [rope_len][32] for the full (global) and sliding frequencies
+  DevBuf cos_full, sin_full, cos_slide, sin_slide;
+  int rope_len = 0;
+
+  // arena
+  int cap_rows = 0, cap_mk = 0, cap_n = 0;
+  uint64_t arena_gen = 0;  // bumped on every reallocation; captured graphs record it
+  DevBuf x, t16, qkv, ctx, gate, hmlp, mk16, partial, out_logits, out_act, err, plan_buf;
+  CUtensorMap tm_t16, tm_ctx, tm_gate, tm_hmlp, tm_mk;
+  uint8_t* staging = nullptr;    // pinned host staging for plan uploads
+  size_t staging_bytes = 0;
+  float* pinned_out = nullptr;   // pinned staging for outputs
+  size_t pinned_out_floats = 0;
+
+  // launch profiling (laya_plan_profile): an event after every launch
+  enum ProfKind { kProfQkv, kProfWo, kProfWi, kProfWo2, kProfHead, kProfAttn, kProfNorm, kProfTail };
+  std::vector<cudaEvent_t>* prof_ev = nullptr;
+  std::vector<int>* prof_kind = nullptr;
+
+  void mark(int kind) {
+    if (!prof_ev) return;
+    cudaEvent_t ev;
+    ck(cudaEventCreate(&ev), "event create");
+    prof_ev->push_back(ev);
+    prof_kind->push_back(kind);
+    ck(cudaEventRecord(ev, stream), "event record");
+  }
+
+  ~Engine() {
+    if (stream) cudaStreamSynchronize(stream);
+    if (pinned_out) cudaFreeHost(pinned_out);
+    if (staging) cudaFreeHost(staging);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  void set_device() { ck(cudaSetDevice(device), "cudaSetDevice"); }
+
+  const Weight& W(const std::string& name) const {
+    auto it = w.find(name);
+    if (it == w.end() || !it->second.present) throw Error(LAYA_E_STATE, "weight " + name + " was not loaded");
+    return it->second;
+  }
+
+  // ---- weights ------------------------------------------------------------------
+  void upload(const std::string& name, const void* data, bool is_f16, const int64_t* dims, int nd) {
+    auto it = roles().find(name);
+    if (it == roles().end()) throw Error(LAYA_E_LOAD, "unknown tensor name " + name);
+    const Role& role = it->second;
+    std::vector<int64_t> got(dims, dims + nd);
+    if (got != role.shape) {
+      std::string g, e;
+      for (auto d : got) g += std::to_string(d) + ",";
+      for (auto d : role.shape) e += std::to_string(d) + ",";
+      throw Error(LAYA_E_LOAD, "tensor " + name + " has stored shape [" + g + "] but this build pins [" + e + "]");
+    }
+    size_t el = 1;
+    for (auto d : got) el *= (size_t)d;
+    auto f32_at = [&](size_t i) {
+      return is_f16 ? h2f_bits(static_cast<const uint16_t*>(data)[i]) : static_cast<const float*>(data)[i];
+    };
+    Weight& wt = w[name];
+    switch (role.kind) {
+      case Kind::Linear:
+      case Kind::Embed:
+      case Kind::ActW1: {
+        std::vector<uint16_t> h;
+        const bool wi = name.find(".mlp.Wi.weight") != std::string::npos;
+        if (wi) {
+          // Gate/up co-tiling for the fused GeGLU epilogue: output tile j
+          // (256 rows) holds gate rows 128j..128j+127 then the matching up
+          // rows 2624+128j..; rows past 2624 in a half are zero.
+          h.assign((size_t)2 * INTER_PAD * H, 0);
+          for (int j = 0; j < INTER_PAD / 128; ++j)
+            for (int r = 0; r < 128; ++r) {
+              const int g = 128 * j + r;
+              if (g >= INTER) continue;
+              for (int c = 0; c < H; ++c) {
+                h[((size_t)256 * j + r) * H + c] = f2h_or_copy(data, is_f16, (size_t)g * H + c);
+                h[((size_t)256 * j + 128 + r) * H + c] = f2h_or_copy(data, is_f16, (size_t)(INTER + g) * H + c);
+              }
+            }
+        } else {
+          h.resize(el);
+          for (size_t i = 0; i < el; ++i) h[i] = f2h_or_copy(data, is_f16, i);
+        }
+        wt.buf.alloc(h.size() * 2, "weight alloc");
+        ck(cudaMemcpy(wt.buf.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+        if (role.kind == Kind::Linear) {
+          const uint64_t rows = wi ? (uint64_t)2 * INTER_PAD : (uint64_t)role.shape[0];
+          const uint64_t kdim = (uint64_t)role.shape[1];
+          if (make_tmap_f16(&wt.tmap, wt.buf.p, rows, kdim, kGemmBN) != 0)
+            throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
+        }
+        break;
+      }
+      case Kind::F32Vec:
+      case Kind::F32Mat:
+      case Kind::Rope: {
+        std::vector<float> f(el);
+        for (size_t i = 0; i < el; ++i) f[i] = f32_at(i);
+        wt.buf.alloc(el * 4, "weight alloc");
+        ck(cudaMemcpy(wt.buf.p, f.data(), el * 4, cudaMemcpyHostToDevice), "weight upload");
+        if (role.kind == Kind::Rope || name == "scorer.3.bias") wt.host = f;
+        break;
+      }
+    }
+    wt.present = true;
+  }
+
+  static uint16_t f2h_or_copy(const void* data, bool is_f16, size_t i) {
+    return is_f16 ? static_cast<const uint16_t*>(data)[i] : f2h_bits(static_cast<const float*>(data)[i]);
+  }
+
+  void finalize() {
+    for (const auto& kv : roles()) {
+      auto it = w.find(kv.first);
+      if (it == w.end() || !it->second.present) throw Error(LAYA_E_LOAD, "no tensor named " + kv.first);
+    }
+    finalized = true;
+    ensure_rope(512);
+  }
+
+  // graph.rs:62-84: cos/sin(p * freq[j]) in f32 with libm cosf/sinf.
+  void ensure_rope(int len) {
+    if (len <= rope_len) return;
+    int n = rope_len ? rope_len : 512;
+    while (n < len) n *= 2;
+    const auto& ff = W("rope.freq_full").host;
+    const auto& fs = W("rope.freq_sliding").host;
+    std::vector<float> cf(n * 32), sf(n * 32), cs(n * 32), ss(n * 32);
+    for (int p = 0; p < n; ++p)
+      for (int j = 0; j < 32; ++j) {
+        const float a = (float)p * ff[j];
+        const float b = (float)p * fs[j];
+        cf[p * 32 + j] = cosf(a);
+        sf[p * 32 + j] = sinf(a);
+        cs[p * 32 + j] = cosf(b);
+        ss[p * 32 + j] = sinf(b);
+      }
+    ck(cudaStreamSynchronize(stream), "sync");
+    for (auto* pr : {&cos_full, &sin_full, &cos_slide, &sin_slide}) pr->alloc((size_t)n * 32 * 4, "rope alloc");
+    ck(cudaMemcpy(cos_full.p, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    ck(cudaMemcpy(sin_full.p, sf.data(), sf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    ck(cudaMemcpy(cos_slide.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    ck(cudaMemcpy(sin_slide.p, ss.data(), ss.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    rope_len = n;
+  }
+
+  // ---- arena ----------------------------------------------------------------------
+  void ensure_arena(const HostPlan& p) {
+    ensure_rope(p.l);
+    const int rows = (p.R + kGemmBM - 1) / kGemmBM * kGemmBM;
+    const int mk = (p.n * p.k + kGemmBM - 1) / kGemmBM * kGemmBM;
+    if (rows <= cap_rows && mk <= cap_mk && p.n <= cap_n) return;
+    ck(cudaStreamSynchronize(stream), "sync");
+    cap_rows = std::max(rows, cap_rows);
+    cap_mk = std::max(mk, cap_mk);
+    cap_n = std::max(p.n, cap_n);
+    ++arena_gen;
+    const size_t R = cap_rows;
+    x.alloc(R * H * 4, "arena x");
+    t16.alloc(R * H * 2, "arena t16");
+    qkv.alloc(R * 3 * H * 2, "arena qkv");
+    ctx.alloc(R * H * 2, "arena ctx");
+    gate.alloc(R * INTER * 2, "arena gate");
+    hmlp.alloc(R * HEAD_INTER * 2, "arena hmlp");
+    mk16.alloc((size_t)cap_mk * H * 2, "arena markers");
+    partial.alloc((size_t)(H / kGemmBN) * cap_mk * 4, "arena partial");
+    out_logits.alloc((size_t)cap_mk * 4, "arena logits");
+    out_act.alloc((size_t)cap_n * 2 * 4, "arena act");
+    for (DevBuf* b : {&x, &t16, &qkv, &ctx, &gate, &hmlp, &mk16, &partial})
+      ck(cudaMemset(b->p, 0, b->bytes), "arena clear");
+    if (make_tmap_f16(&tm_t16, t16.p, R, H, kGemmBM) || make_tmap_f16(&tm_ctx, ctx.p, R, H, kGemmBM) ||
+        make_tmap_f16(&tm_gate, gate.p, R, INTER, kGemmBM) ||
+        make_tmap_f16(&tm_hmlp, hmlp.p, R, HEAD_INTER, kGemmBM) ||
+        make_tmap_f16(&tm_mk, mk16.p, cap_mk, H, kGemmBM))
+      throw Error(LAYA_E_CUDA, "tensor map encode failed for the arena");
+  }
+
+  // ---- the forward ---------------------------------------------------------------
+  void gemm(int epi, const CUtensorMap& A, const Weight& Wt, int M, int N, int K, GemmArgs a, int64_t& nl,
+            int kind) {
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.err = err.as<int>();
+    ck(launch_gemm(epi, &A, &Wt.tmap, a, num_sms, stream), "gemm launch");
+    ++nl;
+    mark(kind);
+  }
+
+  // Enqueues one forward of plan `dp` on the stream (graph.rs:86-186).
+  int64_t enqueue(const DevicePlan& dp, laya_tap_fn tap = nullptr, void* user = nullptr) {
+    const HostPlan& p = dp.host;
+    const PlanLayout& L = dp.lay;
+    const int R = p.R;
+    const int* tok = dp.at<int>(L.tok);
+    const int* pos = dp.at<int>(L.pos);
+    int64_t nl = 0;
+    AttnArgs aa{qkv.as<__half>(), ctx.as<__half>(), dp.at<int>(L.seq_start), dp.at<int>(L.seq_len),
+                dp.at<int2>(L.blocks), -1};
+
+    ck(launch_embed_ln(W("encoder.embeddings.tok_embeddings.weight").buf.as<__half>(), tok,
+                       W(attn_norm(0)).buf.as<float>(), EPS, x.as<float>(), t16.as<__half>(), R, stream),
+       "embed_ln");
+    ++nl;
+    mark(kProfNorm);
+    for (int layer = 0; layer < NLAYER; ++layer) {
+      const bool global = layer % GLOBAL_EVERY == 0;
+      if (layer > 0) {
+        ck(launch_ln(x.as<float>(), nullptr, W(attn_norm(layer)).buf.as<float>(), nullptr, EPS, t16.as<__half>(), R,
+                     stream),
+           "ln");
+        ++nl;
+        mark(kProfNorm);
+      }
+      GemmArgs g{};
+      g.out = qkv.p;
+      g.ldo = 3 * H;
+      g.pos = pos;
+      g.cosb = global ? cos_full.as<float>() : cos_slide.as<float>();
+      g.sinb = global ? sin_full.as<float>() : sin_slide.as<float>();
+      g.scale = SCALE;
+      gemm(kEpiQkvRope, tm_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), R, 3 * H, H, g, nl,
+           kProfQkv);
+      aa.window = global ? -1 : WINDOW;
+      ck(launch_attention(aa, p.nblocks, stream), "attention");
+      ++nl;
+      mark(kProfAttn);
+      GemmArgs r{};
+      r.out = x.p;
+      r.ldo = H;
+      gemm(kEpiResid, tm_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), R, H, H, r, nl, kProfWo);
+      ck(launch_ln(x.as<float>(), nullptr, W(fmt("encoder.layers.%d.mlp_norm.weight", layer)).buf.as<float>(),
+                   nullptr, EPS, t16.as<__half>(), R, stream),
+         "ln");
+      ++nl;
+      mark(kProfNorm);
+      GemmArgs gg{};
+      gg.out = gate.p;
+      gg.ldo = INTER;
+      gg.n_valid = INTER;
+      gemm(kEpiGeglu, tm_t16, W(fmt("encoder.layers.%d.mlp.Wi.weight", layer)), R, 2 * INTER_PAD, H, gg, nl,
+           kProfWi);
+      gemm(kEpiResid, tm_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), R, H, INTER, r, nl, kProfWo2);
+      if (tap) emit_rows(dp, fmt("enc.%d", layer).c_str(), tap, user);
+    }
+    auto hn = [](int i, const char* s) { return fmt("head.layers.%d.%s", i, s); };
+    ck(launch_final_ln(x.as<float>(), W("encoder.final_norm.weight").buf.as<float>(),
+                       W("type_emb.weight").buf.as<__half>(), dp.at<uint8_t>(L.rowtype),
+                       W(hn(0, "norm1.weight")).buf.as<float>(), W(hn(0, "norm1.bias")).buf.as<float>(), EPS,
+                       t16.as<__half>(), R, stream),
+       "final_ln");
+    ++nl;
+    mark(kProfNorm);
+    if (tap) emit_rows(dp, "final", tap, user);
+    for (int hl = 0; hl < HEAD_LAYERS; ++hl) {
+      if (hl > 0) {
+        ck(launch_ln(x.as<float>(), nullptr, W(hn(hl, "norm1.weight")).buf.as<float>(),
+                     W(hn(hl, "norm1.bias")).buf.as<float>(), EPS, t16.as<__half>(), R, stream),
+           "ln");
+        ++nl;
+        mark(kProfNorm);
+      }
+      GemmArgs g{};
+      g.out = qkv.p;
+      g.ldo = 3 * H;
+      g.bias = W(hn(hl, "self_attn.in_proj_bias")).buf.as<float>();
+      g.scale = SCALE;
+      gemm(kEpiQkvBias, tm_t16, W(hn(hl, "self_attn.in_proj_weight")), R, 3 * H, H, g, nl, kProfHead);
+      aa.window = -1;
+      ck(launch_attention(aa, p.nblocks, stream), "attention");
+      ++nl;
+      mark(kProfAttn);
+      GemmArgs r{};
+      r.out = x.p;
+      r.ldo = H;
+      r.bias = W(hn(hl, "self_attn.out_proj.bias")).buf.as<float>();
+      gemm(kEpiResid, tm_ctx, W(hn(hl, "self_attn.out_proj.weight")), R, H, H, r, nl, kProfHead);
+      ck(launch_ln(x.as<float>(), nullptr, W(hn(hl, "norm2.weight")).buf.as<float>(),
+                   W(hn(hl, "norm2.bias")).buf.as<float>(), EPS, t16.as<__half>(), R, stream),
+         "ln");
+      ++nl;
+      mark(kProfNorm);
+      GemmArgs f{};
+      f.out = hmlp.p;
+      f.ldo = HEAD_INTER;
+      f.bias = W(hn(hl, "linear1.bias")).buf.as<float>();
+      gemm(kEpiBiasRelu, tm_t16, W(hn(hl, "linear1.weight")), R, HEAD_INTER, H, f, nl, kProfHead);
+      GemmArgs r2{};
+      r2.out = x.p;
+      r2.ldo = H;
+      r2.bias = W(hn(hl, "linear2.bias")).buf.as<float>();
+      gemm(kEpiResid, tm_hmlp, W(hn(hl, "linear2.weight")), R, H, HEAD_INTER, r2, nl, kProfHead);
+      if (tap) emit_rows(dp, fmt("head.%d", hl).c_str(), tap, user);
+    }
+    const int nk = p.n * p.k;
+    ck(launch_ln(x.as<float>(), dp.at<int>(L.mk_row), W("scorer.0.weight").buf.as<float>(),
+                 W("scorer.0.bias").buf.as<float>(), EPS, mk16.as<__half>(), nk, stream),
+       "scorer ln");
+    ++nl;
+    mark(kProfNorm);
+    GemmArgs s{};
+    s.out = partial.p;
+    s.ldo = cap_mk;
+    s.bias = W("scorer.1.bias").buf.as<float>();
+    s.wvec = W("scorer.3.weight").buf.as<float>();
+    gemm(kEpiScorer, tm_mk, W("scorer.1.weight"), nk, H, H, s, nl, kProfHead);
+    TailArgs t{};
+    t.partial = partial.as<float>();
+    t.ldp = cap_mk;
+    t.score_bias = W("scorer.3.bias").host[0];
+    t.mmask = dp.at<int8_t>(L.mmask);
+    t.cls_row = dp.at<int>(L.cls_row);
+    t.x = x.as<float>();
+    t.w1 = W("act_head.0.weight").buf.as<__half>();
+    t.b1 = W("act_head.0.bias").buf.as<float>();
+    t.w2 = W("act_head.2.weight").buf.as<float>();
+    t.b2 = W("act_head.2.bias").buf.as<float>();
+    t.logits = out_logits.as<float>();
+    t.act = out_act.as<float>();
+    t.n = p.n;
+    t.k = p.k;
+    ck(launch_tail(t, stream), "tail");
+    ++nl;
+    mark(kProfTail);
+    return nl;
+  }
+
+  // Diagnostic: copies the residual stream back and scatters it to padded rows.
+  void emit_rows(const DevicePlan& dp, const char* stage, laya_tap_fn tap, void* user) {
+    const HostPlan& p = dp.host;
+    std::vector<float> c((size_t)p.R * H), o((size_t)p.n * p.l * H, 0.0f);
+    ck(cudaMemcpyAsync(c.data(), x.p, c.size() * 4, cudaMemcpyDeviceToHost, stream), "tap copy");
+    ck(cudaStreamSynchronize(stream), "tap sync");
+    for (int b = 0; b < p.n; ++b)
+      memcpy(&o[(size_t)b * p.l * H], &c[(size_t)p.seq_start[b] * H], (size_t)p.seq_len[b] * H * 4);
+    tap(user, stage, o.data(), o.size());
+  }
+
+  // Packs the plan into pinned staging and copies it to device memory.  The
+  // staging buffer is reused: every caller synchronizes the stream before
+  // the next upload (plan_create here, forward in read_outputs).
+  void upload_plan(DevicePlan& dp, bool use_engine_buffer) {
+    dp.lay = layout_for(dp.host);
+    if (staging_bytes < dp.lay.total) {
+      ck(cudaStreamSynchronize(stream), "sync");
+      if (staging) cudaFreeHost(staging);
+      staging = nullptr;
+      staging_bytes = 0;
+      ck(cudaMallocHost(&staging, dp.lay.total * 2), "pinned staging");
+      staging_bytes = dp.lay.total * 2;
+    }
+    pack(dp.host, dp.lay, staging);
+    if (use_engine_buffer) {
+      if (plan_buf.bytes < dp.lay.total) {
+        ck(cudaStreamSynchronize(stream), "sync");
+        plan_buf.alloc(dp.lay.total * 2, "plan buffer");
+      }
+      dp.base = plan_buf.as<uint8_t>();
+    } else {
+      dp.own.alloc(dp.lay.total, "plan buffer");
+      dp.base = dp.own.as<uint8_t>();
+    }
+    ck(cudaMemcpyAsync(dp.base, staging, dp.lay.total, cudaMemcpyHostToDevice, stream), "plan upload");
+    if (!use_engine_buffer) ck(cudaStreamSynchronize(stream), "plan upload sync");
+  }
+
+  // Runs the plan `steps` times with an event after every launch; sums the
+  // device time between consecutive events per launch kind.
+  void profile(DevicePlan& dp, int steps, double* ms, int64_t* launches) {
+    for (int i = 0; i < 8; ++i) {
+      ms[i] = 0;
+      launches[i] = 0;
+    }
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> kind;
+    prof_ev = &ev;
+    prof_kind = &kind;
+    try {
+      for (int s = 0; s < steps; ++s) {
+        mark(-1);
+        enqueue(dp);
+      }
+      prof_ev = nullptr;
+      prof_kind = nullptr;
+      ck(cudaStreamSynchronize(stream), "profile sync");
+      for (size_t i = 1; i < ev.size(); ++i) {
+        if (kind[i] < 0) continue;
+        float t = 0;
+        ck(cudaEventElapsedTime(&t, ev[i - 1], ev[i]), "event elapsed");
+        ms[kind[i]] += t;
+        launches[kind[i]] += 1;
+      }
+    } catch (...) {
+      prof_ev = nullptr;
+      prof_kind = nullptr;
+      cudaStreamSynchronize(stream);
+      for (auto e : ev) cudaEventDestroy(e);
+      throw;
+    }
+    for (auto e : ev) cudaEventDestroy(e);
+  }
+
+  void check_device_error() {
+    int e = 0;
+    ck(cudaMemcpyAsync(&e, err.p, sizeof(int), cudaMemcpyDeviceToHost, stream), "error word read");
+    ck(cudaStreamSynchronize(stream), "forward sync");
+    if (e != 0) {
+      ck(cudaMemsetAsync(err.p, 0, sizeof(int), stream), "error word reset");
+      ck(cudaStreamSynchronize(stream), "sync");
+      throw Error(LAYA_E_DEVICE_TIMEOUT, fmt("a device-side wait expired (code %d)", e));
+    }
+  }
+
+  void read_outputs(const HostPlan& p, float* logits, float* act) {
+    const size_t nl = (size_t)p.n * p.k, na = (size_t)p.n * 2;
+    if (pinned_out_floats < nl + na) {
+      if (pinned_out) cudaFreeHost(pinned_out);
+      pinned_out = nullptr;
+      ck(cudaMallocHost(&pinned_out, (nl + na) * 4), "pinned alloc");
+      pinned_out_floats = nl + na;
+    }
+    ck(cudaMemcpyAsync(pinned_out, out_logits.p, nl * 4, cudaMemcpyDeviceToHost, stream), "logits copy");
+    ck(cudaMemcpyAsync(pinned_out + nl, out_act.p, na * 4, cudaMemcpyDeviceToHost, stream), "act copy");
+    check_device_error();
+    memcpy(logits, pinned_out, nl * 4);
+    memcpy(act, pinned_out + nl, na * 4);
+  }
+
+  void forward(const laya_req* q, float* logits, float* act, laya_tap_fn tap, void* user) {
+    if (!finalized) throw Error(LAYA_E_STATE, "engine has no weights (call laya_finalize)");
+    if (!logits || !act) throw Error(LAYA_E_INVALID, "null output buffer");
+    set_device();
+    DevicePlan dp;
+    dp.host = make_plan(q);
+    ensure_arena(dp.host);
+    upload_plan(dp, true);
+    enqueue(dp, tap, user);
+    read_outputs(dp.host, logits, act);
+    if (tap) {
+      tap(user, "logits", logits, (size_t)dp.host.n * dp.host.k);
+      tap(user, "act", act, (size_t)dp.host.n * 2);
+    }
+  }
+};
+
+void load_gguf(Engine& e, const std::string& path) {
+  GgufFile g(path);
+  // ModelMeta::from_header (weights.rs:138-222)
+  const GgufValue* arch = g.get("general.architecture");
+  if (!arch || !arch->has_s || arch->s != "laya")
+    throw Error(LAYA_E_LOAD, fmt("%s: general.architecture is %s, want \"laya\"", path.c_str(),
+                                 arch && arch->has_s ? ("\"" + arch->s + "\"").c_str() : "\"\""));
+  const std::pair<const char*, uint64_t> nums[] = {
+      {"laya.hidden_size", H},         {"laya.num_layers", NLAYER},       {"laya.num_heads", NH},
+      {"laya.head_dim", HD},           {"laya.intermediate_size", INTER}, {"laya.vocab_size", NVOCAB},
+      {"laya.sliding_window", WINDOW}, {"laya.global_layer_every", GLOBAL_EVERY},
+      {"laya.head_layers", HEAD_LAYERS}, {"laya.act_input_features", ACT_INPUT},
+      {"laya.question_types", QTYPES}, {"laya.max_len", 512}, {"laya.head_max_len", 192},
+      {"laya.max_prefixes", 6}};
+  for (const auto& kv : nums) {
+    const GgufValue* v = g.get(kv.first);
+    if (!v) throw Error(LAYA_E_LOAD, fmt("%s: missing metadata %s", path.c_str(), kv.first));
+    if (!v->has_u) throw Error(LAYA_E_LOAD, fmt("%s: metadata %s is not an integer", path.c_str(), kv.first));
+    if (v->u != kv.second)
+      throw Error(LAYA_E_LOAD, fmt("%s: metadata %s is %llu but this build pins %llu", path.c_str(), kv.first,
+                                   (unsigned long long)v->u, (unsigned long long)kv.second));
+  }
+  const std::pair<const char*, float> flts[] = {{"laya.attention_scale", SCALE}, {"laya.layer_norm_epsilon", EPS}};
+  for (const auto& kv : flts) {
+    const GgufValue* v = g.get(kv.first);
+    if (!v) throw Error(LAYA_E_LOAD, fmt("%s: missing metadata %s", path.c_str(), kv.first));
+    if (!v->has_f) throw Error(LAYA_E_LOAD, fmt("%s: metadata %s is not a float", path.c_str(), kv.first));
+    const float got = (float)v->f;
+    uint32_t gb, wb;
+    memcpy(&gb, &got, 4);
+    memcpy(&wb, &kv.second, 4);
+    if (gb != wb)
+      throw Error(LAYA_E_LOAD, fmt("%s: metadata %s is %g but this build pins %g", path.c_str(), kv.first, got,
+                                   kv.second));
+  }
+  for (int i = 0; i < 3; ++i) {
+    const GgufValue* v = g.get(fmt("laya.temperature.%d", i));
+    if (!v || !v->has_f) throw Error(LAYA_E_LOAD, fmt("%s: missing metadata laya.temperature.%d", path.c_str(), i));
+    e.temperature[i] = (float)v->f;
+  }
+  if (const GgufValue* v = g.get("laya.temperature_by_options"); v && v->has_s) e.temperature_by_options = v->s;
+  if (const GgufValue* v = g.get("general.file_type"); v && v->has_u) e.file_type = (int)v->u;
+  if (e.file_type != 0 && e.file_type != 1)
+    throw Error(LAYA_E_LOAD, fmt("general.file_type is %d, but this build only handles 0 (F32) and 1 (mostly F16)",
+                                 e.file_type));
+  std::vector<uint8_t> bytes;
+  for (const auto& kv : roles()) {
+    const GgufTensor* t = g.tensor(kv.first);
+    if (!t) throw Error(LAYA_E_LOAD, path + ": no tensor named " + kv.first);
+    if (t->ty != 0 && t->ty != 1 && t->ty != 30)
+      throw Error(LAYA_E_LOAD, fmt("%s: tensor %s has type %u, which this build does not decode", path.c_str(),
+                                   kv.first.c_str(), t->ty));
+    bytes.resize(t->nbytes());
+    g.read_bytes(*t, bytes.data());
+    auto sd = t->stored_dims();
+    if (t->ty == 30) {  // bf16 -> f32 (gguf.rs:560-563)
+      std::vector<float> f(t->elems());
+      const uint16_t* b = reinterpret_cast<const uint16_t*>(bytes.data());
+      for (size_t i = 0; i < f.size(); ++i) {
+        uint32_t u = (uint32_t)b[i] << 16;
+        memcpy(&f[i], &u, 4);
+      }
+      e.upload(kv.first, f.data(), false, sd.data(), (int)sd.size());
+    } else {
+      e.upload(kv.first, bytes.data(), t->ty == 1, sd.data(), (int)sd.size());
+    }
+  }
+  e.finalize();
+}
+
+Engine* open_engine(int device) {
+  int n = 0;
+  ck(cudaGetDeviceCount(&n), "cudaGetDeviceCount");
+  if (device < 0 || device >= n) throw Error(LAYA_E_INVALID, fmt("device %d out of range (%d devices)", device, n));
+  std::unique_ptr<Engine> e(new Engine());
+  e->device = device;
+  e->set_device();
+  cudaDeviceProp prop;
+  ck(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+  if (prop.major != 10)
+    throw Error(LAYA_E_CUDA, fmt("device %d is sm_%d%d; this build targets sm_100a (B200)", device, prop.major,
+                                 prop.minor));
+  e->device_name = prop.name;
+  e->num_sms = prop.multiProcessorCount;
+  ck(cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking), "stream create");
+  e->err.alloc(256, "error word");
+  ck(cudaMemset(e->err.p, 0, 256), "error word clear");
+  return e.release();
+}
+
+}  // namespace laya
+
+using laya::Engine;
+using laya::Error;
+using laya::guard;
+
+struct laya_engine {
+  Engine* e;
+};
+struct laya_plan {
+  laya::DevicePlan dp;
+};
+
+extern "C" {
+
+const char* laya_last_error(void) { return laya::g_err.c_str(); }
+
+int laya_open(int device, const char* gguf_path, laya_engine** out) {
+  return guard([&] {
+    if (!out || !gguf_path) throw Error(LAYA_E_INVALID, "null argument");
+    *out = nullptr;
+    std::unique_ptr<Engine> e(laya::open_engine(device));
+    laya::load_gguf(*e, gguf_path);
+    *out = new laya_engine{e.release()};
+  });
+}
+
+int laya_open_empty(int device, laya_engine** out) {
+  return guard([&] {
+    if (!out) throw Error(LAYA_E_INVALID, "null argument");
+    *out = new laya_engine{laya::open_engine(device)};
+  });
+}
+
+int laya_upload_weight_f16(laya_engine* e, const char* name, const uint16_t* data, const int64_t* dims, int nd) {
+  return guard([&] {
+    if (!e || !name || !data || !dims || nd <= 0 || nd > 4) throw Error(LAYA_E_INVALID, "bad argument");
+    e->e->set_device();
+    e->e->upload(name, data, true, dims, nd);
+  });
+}
+
+int laya_upload_weight_f32(laya_engine* e, const char* name, const float* data, const int64_t* dims, int nd) {
+  return guard([&] {
+    if (!e || !name || !data || !dims || nd <= 0 || nd > 4) throw Error(LAYA_E_INVALID, "bad argument");
+    e->e->set_device();
+    e->e->upload(name, data, false, dims, nd);
+  });
+}
+
+int laya_finalize(laya_engine* e) {
+  return guard([&] {
+    if (!e) throw Error(LAYA_E_INVALID, "null engine");
+    e->e->set_device();
+    e->e->finalize();
+  });
+}
+
+int laya_forward(laya_engine* e, const laya_req* req, float* logits, float* act) {
+  return guard([&] {
+    if (!e) throw Error(LAYA_E_INVALID, "null engine");
+    e->e->forward(req, logits, act, nullptr, nullptr);
+  });
+}
+
+int laya_forward_tapped(laya_engine* e, const laya_req* req, float* logits, float* act, laya_tap_fn fn,
+                        void* user) {
+  return guard([&] {
+    if (!e || !fn) throw Error(LAYA_E_INVALID, "null argument");
+    e->e->forward(req, logits, act, fn, user);
+  });
+}
+
+int laya_info(laya_engine* e, char* buf, size_t len) {
+  return guard([&] {
+    if (!e || !buf || len == 0) throw Error(LAYA_E_INVALID, "null argument");
+    const Engine& g = *e->e;
+    std::string s = laya::fmt(
+        "{\"id\":\"cuda\",\"device\":\"%s (cuda:%d, %d SMs)\",\"dtype\":\"%s\",\"layers\":%d,"
+        "\"calibration\":{\"temperature\":[%.9g,%.9g,%.9g],\"by_options\":%s}}",
+        g.device_name.c_str(), g.device, g.num_sms, g.file_type == 0 ? "fp32" : "fp16", laya::NLAYER,
+        g.temperature[0], g.temperature[1], g.temperature[2], g.temperature_by_options.c_str());
+    if (s.size() + 1 > len) throw Error(LAYA_E_INVALID, "info buffer too small");
+    memcpy(buf, s.c_str(), s.size() + 1);
+  });
+}
+
+void laya_close(laya_engine* e) {
+  if (!e) return;
+  if (e->e) {
+    cudaSetDevice(e->e->device);
+    delete e->e;
+  }
+  delete e;
+}
+
+int laya_plan_create(laya_engine* e, const laya_req* req, laya_plan** out) {
+  return guard([&] {
+    if (!e || !out) throw Error(LAYA_E_INVALID, "null argument");
+    Engine& g = *e->e;
+    if (!g.finalized) throw Error(LAYA_E_STATE, "engine has no weights (call laya_finalize)");
+    g.set_device();
+    std::unique_ptr<laya_plan> p(new laya_plan());
+    p->dp.host = laya::make_plan(req);
+    g.ensure_arena(p->dp.host);
+    g.upload_plan(p->dp, false);
+    *out = p.release();
+  });
+}
+
+int laya_plan_run(laya_engine* e, laya_plan* p) {
+  return guard([&] {
+    if (!e || !p) throw Error(LAYA_E_INVALID, "null argument");
+    Engine& g = *e->e;
+    g.set_device();
+    g.ensure_arena(p->dp.host);
+    if (p->dp.graph && p->dp.graph_arena_gen != g.arena_gen) {
+      // the arena moved since capture: the graph holds stale pointers
+      cudaGraphExecDestroy(p->dp.graph);
+      p->dp.graph = nullptr;
+    }
+    if (p->dp.graph) {
+      laya::ck(cudaGraphLaunch(p->dp.graph, g.stream), "graph launch");
+    } else {
+      p->dp.launches = g.enqueue(p->dp);
+    }
+  });
+}
+
+int laya_plan_capture(laya_engine* e, laya_plan* p) {
+  return guard([&] {
+    if (!e || !p) throw Error(LAYA_E_INVALID, "null argument");
+    Engine& g = *e->e;
+    g.set_device();
+    g.ensure_arena(p->dp.host);
+    // one eager run first: per-device kernel attributes are set outside capture
+    g.enqueue(p->dp);
+    laya::ck(cudaStreamSynchronize(g.stream), "sync");
+    g.check_device_error();
+    cudaGraph_t graph = nullptr;
+    laya::ck(cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    int64_t nl = 0;
+    try {
+      nl = g.enqueue(p->dp);
+    } catch (...) {
+      cudaStreamEndCapture(g.stream, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    laya::ck(cudaStreamEndCapture(g.stream, &graph), "end capture");
+    if (p->dp.graph) cudaGraphExecDestroy(p->dp.graph);
+    p->dp.graph = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&p->dp.graph, graph, 0);
+    cudaGraphDestroy(graph);
+    laya::ck(ie, "graph instantiate");
+    p->dp.graph_arena_gen = g.arena_gen;
+    p->dp.launches = nl;
+  });
+}
+
+int laya_plan_outputs(laya_engine* e, laya_plan* p, float* logits, float* act) {
+  return guard([&] {
+    if (!e || !p || !logits || !act) throw Error(LAYA_E_INVALID, "null argument");
+    e->e->set_device();
+    e->e->read_outputs(p->dp.host, logits, act);
+  });
+}
+
+int laya_plan_stats(laya_plan* p, int64_t* real_tokens, int64_t* launches, int64_t* upload_bytes) {
+  return guard([&] {
+    if (!p) throw Error(LAYA_E_INVALID, "null plan");
+    if (real_tokens) *real_tokens = p->dp.host.R;
+    if (launches) *launches = p->dp.launches;
+    if (upload_bytes) *upload_bytes = (int64_t)p->dp.lay.total;
+  });
+}
+
+int laya_plan_profile(laya_engine* e, laya_plan* p, int steps, double* ms, int64_t* launches) {
+  return guard([&] {
+    if (!e || !p || !ms || !launches || steps <= 0) throw Error(LAYA_E_INVALID, "bad argument");
+    Engine& g = *e->e;
+    g.set_device();
+    g.ensure_arena(p->dp.host);
+    g.profile(p->dp, steps, ms, launches);
+    g.check_device_error();
+  });
+}
+
+void laya_plan_destroy(laya_plan* p) { delete p; }
+
+void* laya_stream(laya_engine* e) { return e ? (void*)e->e->stream : nullptr; }
+
+int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float* out, int m, int n, int k) {
+  return guard([&] {
+    if (!a || !wt || !out || m <= 0 || n <= 0 || k <= 0 || n % laya::kGemmBN || k % laya::kGemmBK)
+      throw Error(LAYA_E_INVALID, "selftest_gemm: bad shape");
+    laya::ck(cudaSetDevice(device), "cudaSetDevice");
+    int sms = 0;
+    laya::ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "attr");
+    const int mp = (m + laya::kGemmBM - 1) / laya::kGemmBM * laya::kGemmBM;
+    laya::DevBuf da, dw, dout, derr;
+    da.alloc((size_t)mp * k * 2, "a");
+    dw.alloc((size_t)n * k * 2, "w");
+    dout.alloc((size_t)m * n * 4, "out");
+    derr.alloc(256, "err");
+    laya::ck(cudaMemset(da.p, 0, da.bytes), "memset");
+    laya::ck(cudaMemset(derr.p, 0, 256), "memset");
+    laya::ck(cudaMemcpy(da.p, a, (size_t)m * k * 2, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(dw.p, wt, (size_t)n * k * 2, cudaMemcpyHostToDevice), "h2d");
+    CUtensorMap ta, tw;
+    if (laya::make_tmap_f16(&ta, da.p, mp, k, laya::kGemmBM) || laya::make_tmap_f16(&tw, dw.p, n, k, laya::kGemmBN))
+      throw Error(LAYA_E_CUDA, "tensor map encode failed");
+    laya::GemmArgs g{};
+    g.M = m;
+    g.N = n;
+    g.K = k;
+    g.err = derr.as<int>();
+    g.out = dout.p;
+    g.ldo = n;
+    laya::ck(laya::launch_gemm(laya::kEpiStoreF32, &ta, &tw, g, sms, 0), "gemm launch");
+    laya::ck(cudaDeviceSynchronize(), "gemm run");
+    int ev = 0;
+    laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
+    if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("gemm device wait expired (code %d)", ev));
+    laya::ck(cudaMemcpy(out, dout.p, (size_t)m * n * 4, cudaMemcpyDeviceToHost), "d2h");
+  });
+}
+
+int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens, int n, int window, float* out) {
+  return guard([&] {
+    if (!qkv || !lens || !out || n <= 0) throw Error(LAYA_E_INVALID, "selftest_attention: bad argument");
+    laya::ck(cudaSetDevice(device), "cudaSetDevice");
+    std::vector<int> start(n), len(n);
+    std::vector<int2> blocks;
+    int R = 0;
+    for (int b = 0; b < n; ++b) {
+      if (lens[b] <= 0) throw Error(LAYA_E_INVALID, "selftest_attention: empty sequence");
+      start[b] = R;
+      len[b] = lens[b];
+      for (int q0 = 0; q0 < lens[b]; q0 += laya::kAttnQRows) blocks.push_back(make_int2(b, q0));
+      R += lens[b];
+    }
+    laya::DevBuf dq, dout, ds, dl, db;
+    dq.alloc((size_t)R * 3072 * 2, "qkv");
+    dout.alloc((size_t)R * 1024 * 2, "out");
+    ds.alloc(n * 4, "start");
+    dl.alloc(n * 4, "len");
+    db.alloc(blocks.size() * sizeof(int2), "blocks");
+    laya::ck(cudaMemcpy(dq.p, qkv, dq.bytes, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(ds.p, start.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(dl.p, len.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(db.p, blocks.data(), blocks.size() * sizeof(int2), cudaMemcpyHostToDevice), "h2d");
+    laya::AttnArgs a{dq.as<__half>(), dout.as<__half>(), ds.as<int>(), dl.as<int>(), db.as<int2>(), window};
+    laya::ck(laya::launch_attention(a, (int)blocks.size(), 0), "attention launch");
+    laya::ck(cudaDeviceSynchronize(), "attention run");
+    std::vector<uint16_t> h((size_t)R * 1024);
+    laya::ck(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost), "d2h");
+    for (size_t i = 0; i < h.size(); ++i) out[i] = laya::h2f_bits(h[i]);
+  });
+}
+
+}  // extern "C"

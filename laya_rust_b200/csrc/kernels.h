@@ -1,0 +1,91 @@
+// Host-side declarations of the sm_100a kernels' launchers.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace laya {
+
+// ---- tcgen05 GEMM: out = epilogue(A[M,K] . W[N,K]^T) ------------------------
+constexpr int kGemmBM = 128;
+constexpr int kGemmBN = 256;
+constexpr int kGemmBK = 64;
+
+enum GemmEpilogue : int {
+  kEpiQkvRope = 0,  // f16 out [M, 3072]; RoPE (rotate-half) on q,k; q,k scaled
+  kEpiQkvBias = 1,  // f16 out [M, 3072]; + bias; q,k scaled (head layers, no RoPE)
+  kEpiResid = 2,    // f32 x[M, N] += acc (+ bias)
+  kEpiGeglu = 3,    // f16 out [M, n_valid]; tile = 128 gate | 128 up columns
+  kEpiBiasRelu = 4, // f16 out [M, N] = relu(acc + bias)
+  kEpiScorer = 5,   // f32 partial[N/256][ldo] = sum_c gelu(acc + bias) * wvec
+  kEpiStoreF32 = 6, // f32 out [M, N] = acc (tests)
+};
+
+struct GemmArgs {
+  int M;               // valid rows of A and of the output
+  int N;               // rows of W (multiple of 256)
+  int K;               // multiple of 64
+  int* err;            // device error word
+  void* out;
+  int ldo;             // output leading dimension in elements
+  const float* bias;   // [N] or nullptr
+  const int* pos;      // per-row RoPE position
+  const float* cosb;   // [max_len][32]
+  const float* sinb;   // [max_len][32]
+  float scale;         // q/k scale
+  const float* wvec;   // scorer output weights [N]
+  int n_valid;         // valid output columns for kEpiGeglu
+};
+
+// Encodes a 2-D f16 K-major tensor map: rows x k elements, row stride k*2 B,
+// box {64, box_rows}, 128-byte swizzle.  Returns 0 on success.
+int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k,
+                  uint32_t box_rows);
+
+cudaError_t launch_gemm(int epilogue, const CUtensorMap* tmA, const CUtensorMap* tmB,
+                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+
+// ---- attention over compacted sequences ----------------------------------------
+struct AttnArgs {
+  const __half* qkv;    // [R, 3072]
+  __half* out;          // [R, 1024]
+  const int* seq_start; // [n]
+  const int* seq_len;   // [n]
+  const int2* blocks;   // [num_blocks] = (sequence, first query row within it)
+  int window;           // < 0: global
+};
+cudaError_t launch_attention(const AttnArgs& a, int num_blocks, cudaStream_t stream);
+constexpr int kAttnQRows = 64;
+
+// ---- row kernels -----------------------------------------------------------------
+// x[r] = t[r] = LN(emb[tok[r]]) * w ; writes f32 residual and f16 copy
+cudaError_t launch_embed_ln(const __half* emb, const int* tok, const float* w, float eps,
+                            float* x, __half* t16, int rows, cudaStream_t s);
+// t16[r] = LN(x[src(r)]) * w (+ b); src(r) = idx ? idx[r] : r
+cudaError_t launch_ln(const float* x, const int* idx, const float* w, const float* b, float eps,
+                      __half* t16, int rows, cudaStream_t s);
+// x[r] = LN(x[r]) * wf + type[rowtype[r]];  t16[r] = LN(x[r]) * w1 + b1
+cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb,
+                            const uint8_t* rowtype, const float* w1, const float* b1,
+                            float eps, __half* t16, int rows, cudaStream_t s);
+
+// ---- tail: scorer sum, post, act head --------------------------------------------
+struct TailArgs {
+  const float* partial;   // [4][ldp] scorer partial sums
+  int ldp;
+  float score_bias;
+  const int8_t* mmask;    // [n*k]
+  const int* cls_row;     // [n]
+  const float* x;         // [R, 1024] residual stream after the head layers
+  const __half* w1;       // [256, 1028]
+  const float* b1;        // [256]
+  const float* w2;        // [2, 256]
+  const float* b2;        // [2]
+  float* logits;          // [n*k]
+  float* act;             // [n*2]
+  int n, k;
+};
+cudaError_t launch_tail(const TailArgs& a, cudaStream_t s);
+
+}  // namespace laya

@@ -1,0 +1,172 @@
+// Row kernels: embedding gather + LayerNorm, LayerNorm (optionally gathered),
+// and the final norm + type embedding + first head norm.  One warp per
+// 1024-wide row, the row held in registers (32 values per lane), two-pass f32
+// statistics, 512-byte coalesced loads and stores.
+//
+// Reference semantics: embedding (backend/cpu/mod.rs:145-153), layernorm
+// (:155-186, eps 1e-5, weight-only on encoder layers, weight+bias in the head
+// and scorer), add_type (:372-386), gather_markers (:388-398); graph order
+// graph.rs:101-106 (layer 0 normalises the embedding and the normalised value
+// seeds the residual stream, :113-114) and graph.rs:127-137.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace laya {
+
+namespace {
+
+constexpr int HID = 1024;
+constexpr int ROWS_PER_CTA = 8;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Normalises v[32] in place (weight/bias applied by the caller).
+__device__ __forceinline__ void normalize(float (&v)[32], float eps) {
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) s += v[i];
+  const float mean = warp_sum(s) * (1.0f / HID);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float d = v[i] - mean;
+    q += d * d;
+  }
+  const float var = warp_sum(q) * (1.0f / HID);
+  const float rstd = 1.0f / sqrtf(var + eps);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * rstd;
+}
+
+// element index of v[4*i + j] held by `lane`: i*128 + lane*4 + j
+__device__ __forceinline__ void load_f32(const float* row, int lane, float (&v)[32]) {
+  const float4* p = reinterpret_cast<const float4*>(row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = p[i * 32 + lane];
+    v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+  }
+}
+
+__device__ __forceinline__ void store_f32(float* row, int lane, const float (&v)[32]) {
+  float4* p = reinterpret_cast<float4*>(row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i * 32 + lane] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+__device__ __forceinline__ void store_f16(__half* row, int lane, const float (&v)[32]) {
+  uint2* p = reinterpret_cast<uint2*>(row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    __half2 a = __floats2half2_rn(v[4 * i], v[4 * i + 1]);
+    __half2 b = __floats2half2_rn(v[4 * i + 2], v[4 * i + 3]);
+    p[i * 32 + lane] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+}
+
+__device__ __forceinline__ void load_f16(const __half* row, int lane, float (&v)[32]) {
+  const uint2* p = reinterpret_cast<const uint2*>(row);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint2 u = __ldg(p + i * 32 + lane);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    v[4 * i] = a.x; v[4 * i + 1] = a.y; v[4 * i + 2] = b.x; v[4 * i + 3] = b.y;
+  }
+}
+
+__device__ __forceinline__ void scale_shift(float (&v)[32], int lane, const float* w, const float* b) {
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = __ldg(w4 + i * 32 + lane);
+    v[4 * i] *= f.x; v[4 * i + 1] *= f.y; v[4 * i + 2] *= f.z; v[4 * i + 3] *= f.w;
+  }
+  if (b) {
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = __ldg(b4 + i * 32 + lane);
+      v[4 * i] += f.x; v[4 * i + 1] += f.y; v[4 * i + 2] += f.z; v[4 * i + 3] += f.w;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) embed_ln_kernel(const __half* emb, const int* tok, const float* w,
+                                                       float eps, float* x, __half* t16, int rows) {
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float v[32];
+  load_f16(emb + static_cast<size_t>(tok[row]) * HID, lane, v);
+  normalize(v, eps);
+  scale_shift(v, lane, w, nullptr);
+  store_f32(x + static_cast<size_t>(row) * HID, lane, v);
+  store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
+}
+
+__global__ void __launch_bounds__(256) ln_kernel(const float* x, const int* idx, const float* w, const float* b,
+                                                 float eps, __half* t16, int rows) {
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int src = idx ? idx[row] : row;
+  float v[32];
+  load_f32(x + static_cast<size_t>(src) * HID, lane, v);
+  normalize(v, eps);
+  scale_shift(v, lane, w, b);
+  store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
+}
+
+__global__ void __launch_bounds__(256) final_ln_kernel(float* x, const float* wf, const __half* type_emb,
+                                                       const uint8_t* rowtype, const float* w1,
+                                                       const float* b1, float eps, __half* t16,
+                                                       int rows) {
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float* xr = x + static_cast<size_t>(row) * HID;
+  float v[32], te[32];
+  load_f32(xr, lane, v);
+  normalize(v, eps);
+  scale_shift(v, lane, wf, nullptr);
+  load_f16(type_emb + static_cast<size_t>(rowtype[row]) * HID, lane, te);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] += te[i];
+  store_f32(xr, lane, v);
+  normalize(v, eps);
+  scale_shift(v, lane, w1, b1);
+  store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
+}
+
+inline int grid_rows(int rows) { return (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA; }
+
+}  // namespace
+
+cudaError_t launch_embed_ln(const __half* emb, const int* tok, const float* w, float eps, float* x,
+                            __half* t16, int rows, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  embed_ln_kernel<<<grid_rows(rows), 256, 0, s>>>(emb, tok, w, eps, x, t16, rows);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ln(const float* x, const int* idx, const float* w, const float* b, float eps,
+                      __half* t16, int rows, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  ln_kernel<<<grid_rows(rows), 256, 0, s>>>(x, idx, w, b, eps, t16, rows);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb, const uint8_t* rowtype,
+                            const float* w1, const float* b1, float eps, __half* t16, int rows,
+                            cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  final_ln_kernel<<<grid_rows(rows), 256, 0, s>>>(x, wf, type_emb, rowtype, w1, b1, eps, t16, rows);
+  return cudaGetLastError();
+}
+
+}  // namespace laya

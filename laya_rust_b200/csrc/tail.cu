@@ -1,0 +1,110 @@
+// The decision tail: scorer output sum, marker post-processing and the act
+// head, one CTA per sequence.
+//
+// Reference semantics (laya-rust): scorer output projection + bias
+// (graph.rs:166-167), post (backend/cpu/mod.rs:400-451: logits masked to
+// -10000 where mmask == 0, softmax over all k markers, features
+// [top1, top1 - top2, entropy / ln(max(nv,2)), max(nv,2) / 255]), act_input
+// (:453-465: the sequence's first row ++ features), act MLP
+// (graph.rs:171-176: W1 [256,1028] + b1, GELU, W2 [2,256] + b2).
+// The 1024 -> 1024 scorer hidden layer runs in the GEMM (kEpiScorer), which
+// leaves one partial dot product per 256-column tile; they are summed here in
+// a fixed order.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace laya {
+
+namespace {
+
+constexpr int HID = 1024;
+constexpr int AIN = HID + 4;
+constexpr int AH = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void __launch_bounds__(256) tail_kernel(const TailArgs a) {
+  extern __shared__ float sm[];
+  float* ain = sm;             // [1028]
+  float* hid = sm + AIN;       // [256]
+  float* lg = hid + AH;        // [k]
+  const int b = blockIdx.x;
+  const int k = a.k;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+
+  for (int j = tid; j < k; j += blockDim.x) {
+    const int r = b * k + j;
+    float v;
+    if (a.mmask[r] != 0) {
+      v = a.partial[r];
+      for (int nt = 1; nt < HID / 256; ++nt) v += a.partial[static_cast<size_t>(nt) * a.ldp + r];
+      v += a.score_bias;
+    } else {
+      v = -10000.0f;
+    }
+    lg[j] = v;
+    a.logits[r] = v;
+  }
+  const float* xc = a.x + static_cast<size_t>(a.cls_row[b]) * HID;
+  for (int i = tid; i < HID; i += blockDim.x) ain[i] = xc[i];
+  __syncthreads();
+  if (tid == 0) {
+    float mx = -3.4e38f;
+    for (int j = 0; j < k; ++j) mx = fmaxf(mx, lg[j]);
+    float sum = 0.0f;
+    for (int j = 0; j < k; ++j) sum += expf(lg[j] - mx);
+    const float inv = 1.0f / sum;
+    float t1 = -1.0f, t2 = -1.0f, ent = 0.0f;
+    int nv = 0;
+    for (int j = 0; j < k; ++j) {
+      const float p = expf(lg[j] - mx) * inv;
+      if (p > t1) {
+        t2 = t1;
+        t1 = p;
+      } else if (p > t2) {
+        t2 = p;
+      }
+      ent -= p * logf(fmaxf(p, 1e-9f));
+      if (a.mmask[b * k + j] != 0) ++nv;
+    }
+    if (t2 < 0.0f) t2 = 0.0f;
+    const float nn = static_cast<float>(nv < 2 ? 2 : nv);
+    ain[HID] = t1;
+    ain[HID + 1] = t1 - t2;
+    ain[HID + 2] = ent / logf(nn);
+    ain[HID + 3] = nn / 255.0f;
+  }
+  __syncthreads();
+  for (int o = warp; o < AH; o += blockDim.x / 32) {
+    const __half* w = a.w1 + static_cast<size_t>(o) * AIN;
+    float s = 0.0f;
+    for (int i = lane; i < AIN; i += 32) s += __half2float(w[i]) * ain[i];
+    s = warp_sum(s);
+    if (lane == 0) hid[o] = gelu_erf(s + a.b1[o]);
+  }
+  __syncthreads();
+  if (warp < 2) {
+    const float* w = a.w2 + warp * AH;
+    float s = 0.0f;
+    for (int i = lane; i < AH; i += 32) s += w[i] * hid[i];
+    s = warp_sum(s);
+    if (lane == 0) a.act[b * 2 + warp] = s + a.b2[warp];
+  }
+}
+
+}  // namespace
+
+cudaError_t launch_tail(const TailArgs& a, cudaStream_t s) {
+  if (a.n <= 0) return cudaSuccess;
+  const size_t smem = sizeof(float) * (AIN + AH + a.k);
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  tail_kernel<<<a.n, 256, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace laya

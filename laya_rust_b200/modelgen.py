@@ -99,7 +99,7 @@ def write_model(path: str, seed: int = 0, std: float = 0.02) -> str:
         else:
             data = rng.standard_normal(n, dtype=np.float32) * np.float32(std)
         w.add_tensor(name, gdims, gguf.T_F16, gguf.f16_bytes(data))
-    tmp = path + ".tmp"
+    tmp = f"{path}.tmp{os.getpid()}"
     w.write(tmp)
     os.replace(tmp, path)
     return path
