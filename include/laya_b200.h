@@ -116,6 +116,30 @@ void laya_plan_destroy(laya_plan *p);
 /* The cudaStream_t the engine launches on. */
 void *laya_stream(laya_engine *e);
 
+/* ---- decision tail without allocation (no counterpart in the reference) -----
+ * For hosts that cannot call cudaMalloc/cudaFree when they score: a serving
+ * process whose device memory belongs to another allocator's pool, or a
+ * latency-critical loop that cannot take an allocation's device sync.
+ * Runs the scorer (LayerNorm over the gathered marker rows, 1024x1024 + bias,
+ * GELU, 1024 -> 1 + bias), the marker post-processing and the act head -- the
+ * same kernels the forward ends with -- on the caller's device buffers:
+ *   x        f32 [rows, 1024]  final hidden rows (after the head layers)
+ *   cls_row  int32 [n]         row of each sequence's first token
+ *   mk_row   int32 [n*k]       row of each marker (any valid row if masked)
+ *   mmask    int8  [n*k]       nonzero for real markers
+ *   logits   f32 [n*k], act f32 [n*2]   outputs
+ * Its scratch is one static device array sized for n*k <= 2048 rows (about
+ * 4 MiB, resident on every GPU that loads the library); larger calls return
+ * LAYA_E_INVALID.  No device memory is allocated by the call.  All calls share
+ * that array: calls that overlap on the GPU race, so serialize them.  The
+ * first call on a device (and with an engine) does set-up; make it before
+ * any stream capture.  Enqueues on `stream` (a cudaStream_t, NULL for the
+ * default stream) and returns after synchronizing it. */
+#define LAYA_TAIL_STATIC_MAX_ROWS 2048
+int laya_decision_tail_static(laya_engine *e, const float *x, int n, int k, const int32_t *cls_row,
+                              const int32_t *mk_row, const int8_t *mmask, float *logits, float *act,
+                              void *stream);
+
 /* ---- kernel self-tests (no counterpart in the reference) --------------------
  * Host in, host out; used by the GPU tests to check single kernels. */
 /* out[M,N] (f32) = A[M,K] . W[N,K]^T with A, W f16; N % 256 == 0, K % 64 == 0. */

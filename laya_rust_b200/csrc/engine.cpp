@@ -352,6 +352,31 @@ struct Engine {
   std::vector<cudaEvent_t>* prof_ev = nullptr;
   std::vector<int>* prof_kind = nullptr;
 
+  // decision-tail weight pointers, looked up once (see tail_weights)
+  TailWeights tail_cache{};
+  bool tail_cache_ready = false;
+
+  const TailWeights& tail_weights() {
+    if (!tail_cache_ready) {
+      TailWeights t{};
+      t.ln_w = W("scorer.0.weight").buf.as<float>();
+      t.ln_b = W("scorer.0.bias").buf.as<float>();
+      t.hid_tmap = &W("scorer.1.weight").tmap;
+      t.hid_b = W("scorer.1.bias").buf.as<float>();
+      t.wout = W("scorer.3.weight").buf.as<float>();
+      t.bout = W("scorer.3.bias").host[0];
+      t.w1 = W("act_head.0.weight").buf.as<__half>();
+      t.b1 = W("act_head.0.bias").buf.as<float>();
+      t.w2 = W("act_head.2.weight").buf.as<float>();
+      t.b2 = W("act_head.2.bias").buf.as<float>();
+      t.device = device;
+      t.num_sms = num_sms;
+      tail_cache = t;
+      tail_cache_ready = true;
+    }
+    return tail_cache;
+  }
+
   void mark(int kind) {
     if (!prof_ev) return;
     cudaEvent_t ev;
@@ -882,6 +907,21 @@ struct laya_engine {
 struct laya_plan {
   laya::DevicePlan dp;
 };
+
+namespace laya {
+// Fills *out with the engine's decision-tail weights; returns false (with the
+// reason in laya_last_error) when the engine has no weights yet.
+bool engine_tail_weights(laya_engine* e, TailWeights* out, int* status) {
+  *status = guard([&] {
+    if (!e) throw Error(LAYA_E_INVALID, "null engine");
+    if (!e->e->finalized) throw Error(LAYA_E_STATE, "engine has no weights (call laya_finalize)");
+    *out = e->e->tail_weights();
+  });
+  return *status == LAYA_OK;
+}
+
+void set_last_error(const char* msg) { g_err = msg; }
+}  // namespace laya
 
 extern "C" {
 

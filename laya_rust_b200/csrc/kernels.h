@@ -88,4 +88,22 @@ struct TailArgs {
 };
 cudaError_t launch_tail(const TailArgs& a, cudaStream_t s);
 
+// Device pointers of the decision-tail weights an engine holds (scorer
+// LayerNorm, scorer hidden projection and its tensor map, scorer output,
+// act head), for launch paths outside the engine's own forward.
+struct TailWeights {
+  const float* ln_w;
+  const float* ln_b;
+  const CUtensorMap* hid_tmap;
+  const float* hid_b;
+  const float* wout;
+  float bout;
+  const __half* w1;
+  const float* b1;
+  const float* w2;
+  const float* b2;
+  int device;
+  int num_sms;
+};
+
 }  // namespace laya

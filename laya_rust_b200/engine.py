@@ -71,6 +71,7 @@ def lib():
         L.laya_plan_destroy.restype = None
         L.laya_stream.argtypes = [vp]
         L.laya_stream.restype = vp
+        L.laya_decision_tail_static.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp]
         L.laya_selftest_gemm.argtypes = [ctypes.c_int, vp, vp, _f32p, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int]
         L.laya_selftest_attention.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_int32),
@@ -227,6 +228,13 @@ class Engine:
 
     def plan(self, req: Req) -> Plan:
         return Plan(self, req)
+
+    def decision_tail_static(self, x: int, n: int, k: int, cls_row: int, mk_row: int, mmask: int,
+                             logits: int, act: int, stream: int = 0) -> None:
+        """laya_decision_tail_static on caller-owned device buffers (raw device
+        addresses): scorer, post and act head with no device allocation."""
+        _check(lib().laya_decision_tail_static(self._h, x, n, k, cls_row, mk_row, mmask, logits, act,
+                                               stream or None))
 
     def stream(self) -> int:
         return lib().laya_stream(self._h) or 0
