@@ -192,9 +192,21 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), the approximation
+// the reference CPU backend uses (backend/cpu/mod.rs:59-74, there in f64):
+//   erf(x) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-x^2),
+//   t = 1 / (1 + p |x|), odd in x.
+__device__ __forceinline__ float erf_as(float x) {
+  const float ax = fabsf(x);
+  const float t = __fdividef(1.0f, 1.0f + 0.3275911f * ax);
+  const float poly =
+      t * (0.254829592f + t * (-0.284496736f + t * (1.421413741f + t * (-1.453152027f + t * 1.061405429f))));
+  return copysignf(1.0f - poly * __expf(-ax * ax), x);
+}
+
 __device__ __forceinline__ float gelu_erf(float v) {
   // exact-erf GELU (cpu/mod.rs:76-78): 0.5 v (1 + erf(v / sqrt 2))
-  return 0.5f * v * (1.0f + erff(v / 1.4142135381698608f));
+  return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
 }
 
 }  // namespace laya

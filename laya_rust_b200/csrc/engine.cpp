@@ -305,9 +305,18 @@ HostPlan make_plan(const laya_req* q) {
 
 }  // namespace
 
+// Tensor maps over the arena with this plan's exact row counts: TMA loads
+// zero-fill rows past the last real token, TMA stores clip them.
+struct PlanMaps {
+  CUtensorMap a_t16, a_ctx, a_gate, a_hmlp, a_mk;  // GEMM A operands
+  CUtensorMap o_qkv, o_x, o_gate, o_hmlp;          // GEMM outputs
+  uint64_t gen = ~0ull;                            // arena generation encoded for
+};
+
 struct DevicePlan {
   HostPlan host;
   PlanLayout lay;
+  PlanMaps maps;
   DevBuf own;              // the plan's own device copy (laya_plan_create)
   uint8_t* base = nullptr; // where the packed arrays live (own, or the engine's buffer)
   cudaGraphExec_t graph = nullptr;
@@ -341,7 +350,6 @@ struct Engine {
   int cap_rows = 0, cap_mk = 0, cap_n = 0;
   uint64_t arena_gen = 0;  // bumped on every reallocation; captured graphs record it
   DevBuf x, t16, qkv, ctx, gate, hmlp, mk16, partial, out_logits, out_act, err, plan_buf;
-  CUtensorMap tm_t16, tm_ctx, tm_gate, tm_hmlp, tm_mk;
   uint8_t* staging = nullptr;    // pinned host staging for plan uploads
   size_t staging_bytes = 0;
   float* pinned_out = nullptr;   // pinned staging for outputs
@@ -448,7 +456,7 @@ struct Engine {
         if (role.kind == Kind::Linear) {
           const uint64_t rows = wi ? (uint64_t)2 * INTER_PAD : (uint64_t)role.shape[0];
           const uint64_t kdim = (uint64_t)role.shape[1];
-          if (make_tmap_f16(&wt.tmap, wt.buf.p, rows, kdim, kGemmBN) != 0)
+          if (make_tmap_f16(&wt.tmap, wt.buf.p, rows, kdim, kGemmBBoxRows) != 0)
             throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
         }
         break;
@@ -525,32 +533,43 @@ struct Engine {
     gate.alloc(R * INTER * 2, "arena gate");
     hmlp.alloc(R * HEAD_INTER * 2, "arena hmlp");
     mk16.alloc((size_t)cap_mk * H * 2, "arena markers");
-    partial.alloc((size_t)(H / kGemmBN) * cap_mk * 4, "arena partial");
+    partial.alloc((size_t)kScorerPartials * cap_mk * 4, "arena partial");
     out_logits.alloc((size_t)cap_mk * 4, "arena logits");
     out_act.alloc((size_t)cap_n * 2 * 4, "arena act");
     for (DevBuf* b : {&x, &t16, &qkv, &ctx, &gate, &hmlp, &mk16, &partial})
       ck(cudaMemset(b->p, 0, b->bytes), "arena clear");
-    if (make_tmap_f16(&tm_t16, t16.p, R, H, kGemmBM) || make_tmap_f16(&tm_ctx, ctx.p, R, H, kGemmBM) ||
-        make_tmap_f16(&tm_gate, gate.p, R, INTER, kGemmBM) ||
-        make_tmap_f16(&tm_hmlp, hmlp.p, R, HEAD_INTER, kGemmBM) ||
-        make_tmap_f16(&tm_mk, mk16.p, cap_mk, H, kGemmBM))
+  }
+
+  void ensure_maps(DevicePlan& dp) {
+    PlanMaps& m = dp.maps;
+    if (m.gen == arena_gen) return;
+    const uint64_t R = (uint64_t)dp.host.R, nk = (uint64_t)dp.host.n * dp.host.k;
+    const uint32_t ab = kGemmABoxRows, ob = kGemmOutBoxRows;
+    if (make_tmap_f16(&m.a_t16, t16.p, R, H, ab) || make_tmap_f16(&m.a_ctx, ctx.p, R, H, ab) ||
+        make_tmap_f16(&m.a_gate, gate.p, R, INTER, ab) || make_tmap_f16(&m.a_hmlp, hmlp.p, R, HEAD_INTER, ab) ||
+        make_tmap_f16(&m.a_mk, mk16.p, nk, H, ab) || make_tmap_2d(&m.o_qkv, qkv.p, false, R, 3 * H, 64, ob) ||
+        make_tmap_2d(&m.o_x, x.p, true, R, H, 32, ob) || make_tmap_2d(&m.o_gate, gate.p, false, R, INTER, 64, ob) ||
+        make_tmap_2d(&m.o_hmlp, hmlp.p, false, R, HEAD_INTER, 64, ob))
       throw Error(LAYA_E_CUDA, "tensor map encode failed for the arena");
+    m.gen = arena_gen;
   }
 
   // ---- the forward ---------------------------------------------------------------
-  void gemm(int epi, const CUtensorMap& A, const Weight& Wt, int M, int N, int K, GemmArgs a, int64_t& nl,
-            int kind) {
+  void gemm(int epi, const CUtensorMap& A, const Weight& Wt, const CUtensorMap& Out, int M, int N, int K, GemmArgs a,
+            int64_t& nl, int kind) {
     a.M = M;
     a.N = N;
     a.K = K;
     a.err = err.as<int>();
-    ck(launch_gemm(epi, &A, &Wt.tmap, a, num_sms, stream), "gemm launch");
+    ck(launch_gemm(epi, GemmMaps{&A, &Wt.tmap, &Out}, a, num_sms, stream), "gemm launch");
     ++nl;
     mark(kind);
   }
 
   // Enqueues one forward of plan `dp` on the stream (graph.rs:86-186).
-  int64_t enqueue(const DevicePlan& dp, laya_tap_fn tap = nullptr, void* user = nullptr) {
+  int64_t enqueue(DevicePlan& dp, laya_tap_fn tap = nullptr, void* user = nullptr) {
+    ensure_maps(dp);
+    const PlanMaps& M = dp.maps;
     const HostPlan& p = dp.host;
     const PlanLayout& L = dp.lay;
     const int R = p.R;
@@ -581,7 +600,7 @@ struct Engine {
       g.cosb = global ? cos_full.as<float>() : cos_slide.as<float>();
       g.sinb = global ? sin_full.as<float>() : sin_slide.as<float>();
       g.scale = SCALE;
-      gemm(kEpiQkvRope, tm_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), R, 3 * H, H, g, nl,
+      gemm(kEpiQkvRope, M.a_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), M.o_qkv, R, 3 * H, H, g, nl,
            kProfQkv);
       aa.window = global ? -1 : WINDOW;
       ck(launch_attention(aa, p.nblocks, stream), "attention");
@@ -590,7 +609,7 @@ struct Engine {
       GemmArgs r{};
       r.out = x.p;
       r.ldo = H;
-      gemm(kEpiResid, tm_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), R, H, H, r, nl, kProfWo);
+      gemm(kEpiResid, M.a_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), M.o_x, R, H, H, r, nl, kProfWo);
       ck(launch_ln(x.as<float>(), nullptr, W(fmt("encoder.layers.%d.mlp_norm.weight", layer)).buf.as<float>(),
                    nullptr, EPS, t16.as<__half>(), R, stream),
          "ln");
@@ -600,9 +619,10 @@ struct Engine {
       gg.out = gate.p;
       gg.ldo = INTER;
       gg.n_valid = INTER;
-      gemm(kEpiGeglu, tm_t16, W(fmt("encoder.layers.%d.mlp.Wi.weight", layer)), R, 2 * INTER_PAD, H, gg, nl,
-           kProfWi);
-      gemm(kEpiResid, tm_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), R, H, INTER, r, nl, kProfWo2);
+      gemm(kEpiGeglu, M.a_t16, W(fmt("encoder.layers.%d.mlp.Wi.weight", layer)), M.o_gate, R, 2 * INTER_PAD, H, gg,
+           nl, kProfWi);
+      gemm(kEpiResid, M.a_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), M.o_x, R, H, INTER, r, nl,
+           kProfWo2);
       if (tap) emit_rows(dp, fmt("enc.%d", layer).c_str(), tap, user);
     }
     auto hn = [](int i, const char* s) { return fmt("head.layers.%d.%s", i, s); };
@@ -627,7 +647,7 @@ struct Engine {
       g.ldo = 3 * H;
       g.bias = W(hn(hl, "self_attn.in_proj_bias")).buf.as<float>();
       g.scale = SCALE;
-      gemm(kEpiQkvBias, tm_t16, W(hn(hl, "self_attn.in_proj_weight")), R, 3 * H, H, g, nl, kProfHead);
+      gemm(kEpiQkvBias, M.a_t16, W(hn(hl, "self_attn.in_proj_weight")), M.o_qkv, R, 3 * H, H, g, nl, kProfHead);
       aa.window = -1;
       ck(launch_attention(aa, p.nblocks, stream), "attention");
       ++nl;
@@ -636,7 +656,7 @@ struct Engine {
       r.out = x.p;
       r.ldo = H;
       r.bias = W(hn(hl, "self_attn.out_proj.bias")).buf.as<float>();
-      gemm(kEpiResid, tm_ctx, W(hn(hl, "self_attn.out_proj.weight")), R, H, H, r, nl, kProfHead);
+      gemm(kEpiResid, M.a_ctx, W(hn(hl, "self_attn.out_proj.weight")), M.o_x, R, H, H, r, nl, kProfHead);
       ck(launch_ln(x.as<float>(), nullptr, W(hn(hl, "norm2.weight")).buf.as<float>(),
                    W(hn(hl, "norm2.bias")).buf.as<float>(), EPS, t16.as<__half>(), R, stream),
          "ln");
@@ -646,12 +666,12 @@ struct Engine {
       f.out = hmlp.p;
       f.ldo = HEAD_INTER;
       f.bias = W(hn(hl, "linear1.bias")).buf.as<float>();
-      gemm(kEpiBiasRelu, tm_t16, W(hn(hl, "linear1.weight")), R, HEAD_INTER, H, f, nl, kProfHead);
+      gemm(kEpiBiasRelu, M.a_t16, W(hn(hl, "linear1.weight")), M.o_hmlp, R, HEAD_INTER, H, f, nl, kProfHead);
       GemmArgs r2{};
       r2.out = x.p;
       r2.ldo = H;
       r2.bias = W(hn(hl, "linear2.bias")).buf.as<float>();
-      gemm(kEpiResid, tm_hmlp, W(hn(hl, "linear2.weight")), R, H, HEAD_INTER, r2, nl, kProfHead);
+      gemm(kEpiResid, M.a_hmlp, W(hn(hl, "linear2.weight")), M.o_x, R, H, HEAD_INTER, r2, nl, kProfHead);
       if (tap) emit_rows(dp, fmt("head.%d", hl).c_str(), tap, user);
     }
     const int nk = p.n * p.k;
@@ -665,7 +685,7 @@ struct Engine {
     s.ldo = cap_mk;
     s.bias = W("scorer.1.bias").buf.as<float>();
     s.wvec = W("scorer.3.weight").buf.as<float>();
-    gemm(kEpiScorer, tm_mk, W("scorer.1.weight"), nk, H, H, s, nl, kProfHead);
+    gemm(kEpiScorer, M.a_mk, W("scorer.1.weight"), M.a_mk, nk, H, H, s, nl, kProfHead);
     TailArgs t{};
     t.partial = partial.as<float>();
     t.ldp = cap_mk;
@@ -1119,8 +1139,10 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
     laya::ck(cudaMemset(derr.p, 0, 256), "memset");
     laya::ck(cudaMemcpy(da.p, a, (size_t)m * k * 2, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(dw.p, wt, (size_t)n * k * 2, cudaMemcpyHostToDevice), "h2d");
-    CUtensorMap ta, tw;
-    if (laya::make_tmap_f16(&ta, da.p, mp, k, laya::kGemmBM) || laya::make_tmap_f16(&tw, dw.p, n, k, laya::kGemmBN))
+    CUtensorMap ta, tw, to;
+    if (laya::make_tmap_f16(&ta, da.p, m, k, laya::kGemmABoxRows) ||
+        laya::make_tmap_f16(&tw, dw.p, n, k, laya::kGemmBBoxRows) ||
+        laya::make_tmap_2d(&to, dout.p, true, m, n, 32, laya::kGemmOutBoxRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed");
     laya::GemmArgs g{};
     g.M = m;
@@ -1129,7 +1151,7 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
     g.err = derr.as<int>();
     g.out = dout.p;
     g.ldo = n;
-    laya::ck(laya::launch_gemm(laya::kEpiStoreF32, &ta, &tw, g, sms, 0), "gemm launch");
+    laya::ck(laya::launch_gemm(laya::kEpiStoreF32, laya::GemmMaps{&ta, &tw, &to}, g, sms, 0), "gemm launch");
     laya::ck(cudaDeviceSynchronize(), "gemm run");
     int ev = 0;
     laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");

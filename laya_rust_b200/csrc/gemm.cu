@@ -1,4 +1,4 @@
-// Persistent tcgen05 GEMM for sm_100a with fused epilogues.
+// Persistent 2-SM tcgen05 GEMM for sm_100a with fused epilogues.
 //
 //   out = epilogue(A[M,K] . W[N,K]^T)      A, W f16 K-major, f32 accumulate
 //
@@ -9,16 +9,22 @@
 // (:84-102).  Semantics follow the CPU op contract (backend/cpu/mod.rs:80-126,
 // 202-255, 341-370).
 //
-// CTA = 6 warps, one CTA per SM, persistent over 128x256 output tiles:
-//   warp 0      TMA producer: A 128x64 and W 256x64 tiles, 128B swizzle,
-//               into a 4-stage shared-memory ring (48 KB per stage)
-//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//               (M=128, N=256, K=16 per instruction), accumulators in TMEM,
-//               double-buffered (2 x 256 columns) so the epilogue of tile i
-//               overlaps the main loop of tile i+1
-//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns, fused math,
-//               global stores; warp w reads TMEM lanes 32*(w%4)..+31
-// No clusters and no multicast: every CTA loads its own tiles.
+// A cluster of two CTAs (two SMs) owns one 256 x BN output tile at a time and
+// walks the tile list persistently.  CTA r of the pair holds A rows
+// [128r, 128r+128) and W rows [r*BN/2, (r+1)*BN/2) of every k-block; the
+// leader CTA (r = 0) issues tcgen05.mma.cta_group::2 (M=256, N=BN, K=16),
+// which reads both CTAs' shared memory and leaves rows 128r.. of the f32
+// accumulator in CTA r's TMEM.  Per CTA:
+//   warp 0      TMA producer into a 6-stage ring (32 KB per stage for
+//               BN=256); both CTAs' loads complete on the leader's barrier
+//   warp 1      TMEM allocation (both CTAs); MMA issue (leader only);
+//               accumulators double-buffered in TMEM (2 x BN columns)
+//   warps 2-5   epilogue: tcgen05.ld of 32 TMEM lanes, fused math, a
+//               128-byte-swizzled shared staging tile, then a TMA store
+//               (or TMA reduce-add for the f32 residual) of 32 rows at a time
+// No TMA load in this kernel uses multicast; every CTA loads its own operand
+// halves.  The MMA completion signal is delivered to both CTAs of the pair
+// with tcgen05.commit's cluster-multicast form.
 #include <cstdio>
 
 #include "common.cuh"
@@ -28,15 +34,27 @@ namespace laya {
 
 namespace {
 
-constexpr int BM = kGemmBM, BN = kGemmBN, BK = kGemmBK;
-constexpr int STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
-constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
-constexpr int TMEM_COLS = 2 * BN;
+constexpr int BM = kGemmBM;            // 256 rows per cluster tile
+constexpr int BK = kGemmBK;            // 64
+constexpr int CTA_ROWS = BM / 2;       // 128 rows per CTA
+constexpr int EPI_WARPS = 8;           // two per TMEM lane quarter, one per column half
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr int STAGING_BYTES = 4096;    // 32 rows x 128 B
 constexpr int BAR_BYTES = 256;
-constexpr size_t SMEM_BYTES = 1024 + static_cast<size_t>(STAGES) * STAGE_BYTES + BAR_BYTES;
+constexpr size_t SMEM_LIMIT = 232448;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_BYTES = CTA_ROWS * BK * 2;        // 16 KB
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;        // BN=256: 16 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 6 : 8;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr size_t RING = static_cast<size_t>(STAGES) * STAGE_BYTES;
+  static constexpr size_t STAGING = static_cast<size_t>(EPI_WARPS) * STAGING_BYTES;
+  static constexpr size_t SMEM = 1024 + RING + STAGING + BAR_BYTES;
+  static_assert(SMEM <= SMEM_LIMIT, "shared memory budget");
+};
 
 __device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(v); }
 
@@ -45,19 +63,153 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Stores 32 f16 values (packed in 16 words) to 64 contiguous bytes.
-__device__ __forceinline__ void store_32h(__half* dst, const uint32_t (&p)[16]) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) d[i] = make_uint4(p[4 * i], p[4 * i + 1], p[4 * i + 2], p[4 * i + 3]);
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
 
-template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t t_row, int row, int n0) {
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// 2-D TMA load into this CTA's smem whose completion bytes go to the barrier
+// at cluster address `bar` (the leader CTA's barrier).
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* m, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* smem_src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* smem_src, int x, int y) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc2(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish2() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc2(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void umma2_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the barrier at this smem offset in every CTA of the pair
+// when all previously issued MMAs of this thread have completed.
+__device__ __forceinline__ void umma2_commit_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+// Arrives once on this CTA's own barrier when the MMAs have completed.
+__device__ __forceinline__ void umma2_commit_own(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Writes one thread's 128-byte row (8 x 16 B) of a 32-row staging tile laid
+// out the way a SWIZZLE_128B tensor map expects: 16-byte chunk j of row r at
+// r*128 + ((j ^ (r & 7)) * 16).
+__device__ __forceinline__ void stage_row(uint8_t* stage, int r, const uint32_t (&w)[32]) {
+  uint8_t* row = stage + r * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+}
+
+// Half a row (64 B, chunks [8h, 8h+4) of 16 B): used when 32 f16 values
+// fill one half of a 128-byte staging row.
+__device__ __forceinline__ void stage_half_row(uint8_t* stage, int r, int h, const uint32_t (&w)[16]) {
+  uint8_t* row = stage + r * 128;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = 4 * h + j;
+    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  }
+}
+
+// Per-warp epilogue state: one staging buffer, refilled once the previous
+// TMA store from it has read it.  `active` is false for a 32-row slab that
+// lies wholly past the last row (nothing is stored).
+struct Stager {
+  uint8_t* buf;
+  int lane;
+  bool active;
+  __device__ __forceinline__ uint8_t* acquire() {
+    if (lane == 0) bulk_wait_read<0>();
+    __syncwarp();
+    return buf;
+  }
+  __device__ __forceinline__ void store(const CUtensorMap* m, int x, int y, bool reduce) {
+    fence_async_smem();
+    __syncwarp();
+    if (lane == 0 && active) {
+      if (reduce) tma_reduce_add_2d(m, buf, x, y);
+      else tma_store_2d(m, buf, x, y);
+      bulk_commit();
+    }
+  }
+};
+
+// Epilogue of one warp: 32 rows (TMEM lanes) and column half `hc` of the
+// tile, i.e. columns [hc*BN/2, (hc+1)*BN/2) (for GeGLU: output columns
+// [hc*BN/4, (hc+1)*BN/4), from gate and up columns of that range).
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmOut, Stager& st,
+                                              uint32_t t_row, int row0, int row, int n0, int hc) {
   const bool valid = row < a.M;
+  const int r = row - row0;  // row within this warp's 32-row slab
+  const int cb = hc * (BN / 2), ce = cb + BN / 2;
   if constexpr (EPI == kEpiQkvRope) {
     const int part = n0 / 1024;
-    __half* out = static_cast<__half*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + n0;
     if (part < 2) {
       float cs[32], sn[32];
       const int p = valid ? a.pos[row] : 0;
@@ -70,114 +222,107 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t t_row,
         sn[4 * i] = s.x; sn[4 * i + 1] = s.y; sn[4 * i + 2] = s.z; sn[4 * i + 3] = s.w;
       }
 #pragma unroll 1
-      for (int hh = 0; hh < BN / 64; ++hh) {
+      for (int hh = cb / 64; hh < ce / 64; ++hh) {
         uint32_t lo[32], hi[32];
         tmem_ld_32x32b_x32(t_row + hh * 64, lo);
         tmem_ld_32x32b_x32(t_row + hh * 64 + 32, hi);
         tmem_ld_wait();
-        uint32_t plo[16], phi[16];
+        uint32_t w[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           // rotate-half RoPE: d < 32: q*c - q[d+32]*s ; d >= 32: q*c + q[d-32]*s
-          float a0 = u2f(lo[j]), b0 = u2f(hi[j]), a1 = u2f(lo[j + 1]), b1 = u2f(hi[j + 1]);
-          float r0 = (a0 * cs[j] - b0 * sn[j]) * a.scale;
-          float r1 = (a1 * cs[j + 1] - b1 * sn[j + 1]) * a.scale;
-          float s0 = (b0 * cs[j] + a0 * sn[j]) * a.scale;
-          float s1 = (b1 * cs[j + 1] + a1 * sn[j + 1]) * a.scale;
-          plo[j / 2] = pack_half2(r0, r1);
-          phi[j / 2] = pack_half2(s0, s1);
+          const float a0 = u2f(lo[j]), b0 = u2f(hi[j]), a1 = u2f(lo[j + 1]), b1 = u2f(hi[j + 1]);
+          w[j / 2] = pack_half2((a0 * cs[j] - b0 * sn[j]) * a.scale, (a1 * cs[j + 1] - b1 * sn[j + 1]) * a.scale);
+          w[16 + j / 2] = pack_half2((b0 * cs[j] + a0 * sn[j]) * a.scale, (b1 * cs[j + 1] + a1 * sn[j + 1]) * a.scale);
         }
-        if (valid) {
-          store_32h(out + hh * 64, plo);
-          store_32h(out + hh * 64 + 32, phi);
-        }
+        uint8_t* s = st.acquire();
+        stage_row(s, r, w);
+        st.store(tmOut, n0 + hh * 64, row0, false);
       }
     } else {
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_row + c0, v);
+      for (int c0 = cb; c0 < ce; c0 += 64) {
+        uint32_t v0[32], v1[32];
+        tmem_ld_32x32b_x32(t_row + c0, v0);
+        tmem_ld_32x32b_x32(t_row + c0 + 32, v1);
         tmem_ld_wait();
-        uint32_t p[16];
+        uint32_t w[32];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) p[j / 2] = pack_half2(u2f(v[j]), u2f(v[j + 1]));
-        if (valid) store_32h(out + c0, p);
-      }
-    }
-  } else if constexpr (EPI == kEpiQkvBias) {
-    const int part = n0 / 1024;
-    const float sc = part < 2 ? a.scale : 1.0f;
-    __half* out = static_cast<__half*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + n0;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c0, v);
-      tmem_ld_wait();
-      uint32_t p[16];
-      const float* b = a.bias + n0 + c0;
-#pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        p[j / 2] = pack_half2((u2f(v[j]) + __ldg(b + j)) * sc, (u2f(v[j + 1]) + __ldg(b + j + 1)) * sc);
-      if (valid) store_32h(out + c0, p);
-    }
-  } else if constexpr (EPI == kEpiResid) {
-    float* x = static_cast<float*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + n0;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c0, v);
-      tmem_ld_wait();
-      if (valid) {
-        float4* xp = reinterpret_cast<float4*>(x + c0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float4 o = xp[i];
-          float p0 = u2f(v[4 * i]), p1 = u2f(v[4 * i + 1]), p2 = u2f(v[4 * i + 2]),
-                p3 = u2f(v[4 * i + 3]);
-          if (a.bias) {
-            const float* b = a.bias + n0 + c0 + 4 * i;
-            p0 += __ldg(b); p1 += __ldg(b + 1); p2 += __ldg(b + 2); p3 += __ldg(b + 3);
-          }
-          o.x += p0; o.y += p1; o.z += p2; o.w += p3;
-          xp[i] = o;
+        for (int j = 0; j < 32; j += 2) {
+          w[j / 2] = pack_half2(u2f(v0[j]), u2f(v0[j + 1]));
+          w[16 + j / 2] = pack_half2(u2f(v1[j]), u2f(v1[j + 1]));
         }
+        uint8_t* s = st.acquire();
+        stage_row(s, r, w);
+        st.store(tmOut, n0 + c0, row0, false);
       }
+    }
+  } else if constexpr (EPI == kEpiQkvBias || EPI == kEpiBiasRelu) {
+    const float sc = (EPI == kEpiQkvBias && n0 / 1024 < 2) ? a.scale : 1.0f;
+#pragma unroll 1
+    for (int c0 = cb; c0 < ce; c0 += 64) {
+      uint32_t v0[32], v1[32];
+      tmem_ld_32x32b_x32(t_row + c0, v0);
+      tmem_ld_32x32b_x32(t_row + c0 + 32, v1);
+      tmem_ld_wait();
+      const float* b = a.bias + n0 + c0;
+      uint32_t w[32];
+#pragma unroll
+      for (int j = 0; j < 32; j += 2) {
+        float x0 = u2f(v0[j]) + __ldg(b + j), x1 = u2f(v0[j + 1]) + __ldg(b + j + 1);
+        float y0 = u2f(v1[j]) + __ldg(b + 32 + j), y1 = u2f(v1[j + 1]) + __ldg(b + 33 + j);
+        if constexpr (EPI == kEpiBiasRelu) {
+          x0 = fmaxf(x0, 0.0f); x1 = fmaxf(x1, 0.0f); y0 = fmaxf(y0, 0.0f); y1 = fmaxf(y1, 0.0f);
+        } else {
+          x0 *= sc; x1 *= sc; y0 *= sc; y1 *= sc;
+        }
+        w[j / 2] = pack_half2(x0, x1);
+        w[16 + j / 2] = pack_half2(y0, y1);
+      }
+      uint8_t* s = st.acquire();
+      stage_row(s, r, w);
+      st.store(tmOut, n0 + c0, row0, false);
+    }
+  } else if constexpr (EPI == kEpiResid || EPI == kEpiStoreF32) {
+#pragma unroll 1
+    for (int c0 = cb; c0 < ce; c0 += 32) {
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(t_row + c0, v);
+      tmem_ld_wait();
+      if (EPI == kEpiResid && a.bias) {
+        const float* b = a.bias + n0 + c0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(u2f(v[j]) + __ldg(b + j));
+      }
+      uint8_t* s = st.acquire();
+      stage_row(s, r, v);
+      st.store(tmOut, n0 + c0, row0, EPI == kEpiResid);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     const int oc0 = (n0 / BN) * (BN / 2);
-    __half* out = static_cast<__half*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + oc0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN / 2; c0 += 32) {
-      uint32_t g[32], u[32];
-      tmem_ld_32x32b_x32(t_row + c0, g);
-      tmem_ld_32x32b_x32(t_row + BN / 2 + c0, u);
-      tmem_ld_wait();
-      if (oc0 + c0 >= a.n_valid) continue;
-      uint32_t p[16];
+    for (int c0 = cb / 2; c0 < ce / 2; c0 += 64) {
+      if (oc0 + c0 >= a.n_valid) break;
+      uint32_t w[2][16];
 #pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        p[j / 2] = pack_half2(gelu_erf(u2f(g[j])) * u2f(u[j]), gelu_erf(u2f(g[j + 1])) * u2f(u[j + 1]));
-      if (valid) store_32h(out + c0, p);
-    }
-  } else if constexpr (EPI == kEpiBiasRelu) {
-    __half* out = static_cast<__half*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + n0;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c0, v);
-      tmem_ld_wait();
-      uint32_t p[16];
-      const float* b = a.bias + n0 + c0;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(t_row + c0 + 32 * h, g);
+        tmem_ld_32x32b_x32(t_row + BN / 2 + c0 + 32 * h, u);
+        tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 32; j += 2)
-        p[j / 2] = pack_half2(fmaxf(u2f(v[j]) + __ldg(b + j), 0.0f),
-                              fmaxf(u2f(v[j + 1]) + __ldg(b + j + 1), 0.0f));
-      if (valid) store_32h(out + c0, p);
+        for (int j = 0; j < 32; j += 2)
+          w[h][j / 2] = pack_half2(gelu_erf(u2f(g[j])) * u2f(u[j]), gelu_erf(u2f(g[j + 1])) * u2f(u[j + 1]));
+      }
+      uint8_t* s = st.acquire();
+      stage_half_row(s, r, 0, w[0]);
+      stage_half_row(s, r, 1, w[1]);
+      st.store(tmOut, oc0 + c0, row0, false);
     }
-  } else if constexpr (EPI == kEpiScorer) {
+  } else {  // kEpiScorer
     float s = 0.0f;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = cb; c0 < ce; c0 += 32) {
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c0, v);
       tmem_ld_wait();
@@ -186,55 +331,47 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, uint32_t t_row,
 #pragma unroll
       for (int j = 0; j < 32; ++j) s += gelu_erf(u2f(v[j]) + __ldg(b + j)) * __ldg(w + j);
     }
-    if (valid) static_cast<float*>(a.out)[static_cast<size_t>(n0 / BN) * a.ldo + row] = s;
-  } else {  // kEpiStoreF32
-    float* out = static_cast<float*>(a.out) + static_cast<size_t>(valid ? row : 0) * a.ldo + n0;
-#pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + c0, v);
-      tmem_ld_wait();
-      if (valid) {
-        float4* o = reinterpret_cast<float4*>(out + c0);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          o[i] = make_float4(u2f(v[4 * i]), u2f(v[4 * i + 1]), u2f(v[4 * i + 2]), u2f(v[4 * i + 3]));
-      }
-    }
+    if (valid) static_cast<float*>(a.out)[static_cast<size_t>(2 * (n0 / BN) + hc) * a.ldo + row] = s;
   }
 }
 
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
+  using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
-  uint64_t* empty = full + STAGES;
-  uint64_t* tfull = empty + STAGES;
+  uint8_t* sB = smem + C::STAGES * C::A_BYTES;
+  uint8_t* staging = smem + C::RING;
+  uint64_t* full = reinterpret_cast<uint64_t*>(staging + C::STAGING);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
   const int num_m = (args.M + BM - 1) / BM;
   const int num_n = args.N / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = args.K / BK;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
+      mbar_init(&tempty[i], 2 * EPI_WARPS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -243,13 +380,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmOut);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_holder, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc2(tmem_holder, C::TMEM_COLS);
+    tmem_relinquish2();
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  cluster_sync();  // barrier inits and TMEM allocation visible cluster-wide
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
@@ -257,43 +396,40 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t issued_parity[STAGES];
-      uint32_t issued_mask = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % num_m) * BM;
-        const int n0 = (tile / num_m) * BN;
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+        const int m0 = (tile % num_m) * BM + static_cast<int>(rank) * CTA_ROWS;
+        const int n0 = (tile / num_m) * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait,
-                                 abort_flag)) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, kb * BK, m0, &full[stage]);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, kb * BK, n0, &full[stage]);
-          issued_parity[stage] = phase;
-          issued_mask |= 1u << stage;
-          if (++stage == STAGES) {
+          const uint32_t fb = map_to_rank(smem_u32(&full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
+          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, kb * BK, m0, fb);
+          tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, kb * BK, n0, fb);
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
       }
-      // Let every load this thread issued land before the CTA can exit.
-      for (int s = 0; s < STAGES; ++s)
-        if (issued_mask & (1u << s))
-          mbar_wait_bounded(&full[s], issued_parity[s], args.err, kErrGemmTeardownWait, nullptr);
+      if (!ok) {
+        // give loads already in flight time to land before teardown
+        const unsigned long long t0 = global_ns();
+        while (global_ns() - t0 < 2000000ull) __nanosleep(1000);
+      }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (leader && lane == 0) {
       const uint32_t idesc = umma_idesc_f16(BM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t aphase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
         if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, args.err, kErrGemmMmaWait, abort_flag)) {
           ok = false;
           break;
@@ -306,129 +442,150 @@ __global__ void __launch_bounds__(THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sA + stage * A_BYTES);
-          const uint32_t b_addr = smem_u32(sB + stage * B_BYTES);
+          const uint32_t a_addr = smem_u32(sA + stage * C::A_BYTES);
+          const uint32_t b_addr = smem_u32(sB + stage * C::B_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32),
-                     idesc, (kb | k) != 0 ? 1u : 0u);
-          umma_commit(&empty[stage]);
-          if (++stage == STAGES) {
+            umma2_f16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
+                      (kb | k) != 0 ? 1u : 0u);
+          umma2_commit_both(&empty[stage]);
+          if (++stage == C::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        umma2_commit_both(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) aphase ^= 1u;
       }
-      // Every MMA issued by this thread completes before TMEM is released.
-      umma_commit(drain);
+      // every MMA issued here completes before TMEM is released
+      umma2_commit_own(drain);
       mbar_wait_bounded(drain, 0, args.err, kErrGemmTeardownWait, nullptr);
     }
   } else {
-    const int q = warp & 3;
+    const int ew = warp - 2;
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int hc = ew / 4;   // column half of the tile
+    Stager st{staging + ew * STAGING_BYTES, lane, true};
+    const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0), map_to_rank(smem_u32(&tempty[1]), 0)};
     int acc = 0;
     uint32_t aphase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
       int ok = 1;
       if (lane == 0)
         ok = mbar_wait_bounded(&tfull[acc], aphase, args.err, kErrGemmEpilogueWait, abort_flag);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int m0 = (tile % num_m) * BM;
+      const int m0 = (tile % num_m) * BM + static_cast<int>(rank) * CTA_ROWS;
       const int n0 = (tile / num_m) * BN;
-      const int row = m0 + q * 32 + lane;
-      const uint32_t t_row =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_tile<EPI>(args, t_row, row, n0);
+      const int row0 = m0 + q * 32;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      st.active = row0 < args.M;
+      epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
       acc ^= 1;
       if (acc == 0) aphase ^= 1u;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();
+  cluster_sync();  // no CTA of the pair leaves while the other may still use it
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc2(tmem_base, C::TMEM_COLS);
   }
 }
 
-template <int EPI>
-cudaError_t launch_one(const CUtensorMap* tmA, const CUtensorMap* tmB, const GemmArgs& args,
-                       int num_sms, cudaStream_t stream) {
+template <int EPI, int BN>
+cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!configured[dev]) {
-    e = cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(SMEM_BYTES));
+    e = cudaFuncSetAttribute(gemm_tc_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(Cfg<BN>::SMEM));
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
   const int num_tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
   if (num_tiles == 0) return cudaSuccess;
-  const int grid = num_tiles < num_sms ? num_tiles : num_sms;
-  gemm_tc_kernel<EPI><<<grid, THREADS, SMEM_BYTES, stream>>>(*tmA, *tmB, args);
-  return cudaGetLastError();
+  const int max_clusters = num_sms / 2;
+  const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters, 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg<BN>::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI, BN>, *m.a, *m.b, *m.out, args);
 }
 
 }  // namespace
 
-cudaError_t launch_gemm(int epilogue, const CUtensorMap* tmA, const CUtensorMap* tmB,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream) {
-  if (args.N % BN || args.K % BK || args.M < 0) return cudaErrorInvalidValue;
+cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
+  if (args.N % kGemmBN || args.K % BK || args.M < 0 || !m.a || !m.b || !m.out) return cudaErrorInvalidValue;
   switch (epilogue) {
-    case kEpiQkvRope: return launch_one<kEpiQkvRope>(tmA, tmB, args, num_sms, stream);
-    case kEpiQkvBias: return launch_one<kEpiQkvBias>(tmA, tmB, args, num_sms, stream);
-    case kEpiResid: return launch_one<kEpiResid>(tmA, tmB, args, num_sms, stream);
-    case kEpiGeglu: return launch_one<kEpiGeglu>(tmA, tmB, args, num_sms, stream);
-    case kEpiBiasRelu: return launch_one<kEpiBiasRelu>(tmA, tmB, args, num_sms, stream);
-    case kEpiScorer: return launch_one<kEpiScorer>(tmA, tmB, args, num_sms, stream);
-    case kEpiStoreF32: return launch_one<kEpiStoreF32>(tmA, tmB, args, num_sms, stream);
+    case kEpiQkvRope: return launch_one<kEpiQkvRope, kGemmBN>(m, args, num_sms, stream);
+    case kEpiQkvBias: return launch_one<kEpiQkvBias, kGemmBN>(m, args, num_sms, stream);
+    case kEpiResid: return launch_one<kEpiResid, kGemmBN>(m, args, num_sms, stream);
+    case kEpiGeglu: return launch_one<kEpiGeglu, kGemmBN>(m, args, num_sms, stream);
+    case kEpiBiasRelu: return launch_one<kEpiBiasRelu, kGemmBN>(m, args, num_sms, stream);
+    case kEpiScorer: return launch_one<kEpiScorer, kGemmBN>(m, args, num_sms, stream);
+    case kEpiStoreF32: return launch_one<kEpiStoreF32, kGemmBN>(m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
 // ---- tensor maps -------------------------------------------------------------------
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
 static EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = reinterpret_cast<EncodeTiledFn>(p);
   }
   return fn;
 }
 
-int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k,
-                  uint32_t box_rows) {
+int make_tmap_2d(CUtensorMap* map, const void* base, bool f32, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                 uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return -1;
-  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (k * 2) % 16 || k % 64) return -2;
-  cuuint64_t dims[2] = {k, rows};
-  cuuint64_t strides[1] = {k * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  const uint64_t es = f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) || (cols * es) % 16 || box_cols * es != 128 || rows == 0) return -2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * es};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k, uint32_t box_rows) {
+  if (k % 64) return -2;
+  return make_tmap_2d(map, base, false, rows, k, 64, box_rows);
 }
 
 }  // namespace laya

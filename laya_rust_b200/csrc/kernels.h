@@ -8,9 +8,19 @@
 namespace laya {
 
 // ---- tcgen05 GEMM: out = epilogue(A[M,K] . W[N,K]^T) ------------------------
-constexpr int kGemmBM = 128;
+// A 2-CTA cluster computes a kGemmBM x kGemmBN tile; each CTA loads 128 rows of
+// A (TMA box 64 x 128) and kGemmBN/2 rows of W (box 64 x kGemmBN/2).
+constexpr int kGemmBM = 256;
 constexpr int kGemmBN = 256;
 constexpr int kGemmBK = 64;
+constexpr int kGemmABoxRows = 128;
+constexpr int kGemmBBoxRows = kGemmBN / 2;
+// Output tiles leave through 32-row TMA boxes of 128 bytes per row:
+// 64 f16 columns or 32 f32 columns.
+constexpr int kGemmOutBoxRows = 32;
+// The scorer epilogue leaves one partial dot product per (256-column tile,
+// column half) of its 1024 outputs.
+constexpr int kScorerPartials = 2 * (1024 / kGemmBN);
 
 enum GemmEpilogue : int {
   kEpiQkvRope = 0,  // f16 out [M, 3072]; RoPE (rotate-half) on q,k; q,k scaled
@@ -42,9 +52,22 @@ struct GemmArgs {
 // box {64, box_rows}, 128-byte swizzle.  Returns 0 on success.
 int make_tmap_f16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t k,
                   uint32_t box_rows);
+// General 2-D row-major map (f16 or f32) with a 128-byte-wide box
+// (box_cols * element size == 128) and 128-byte swizzle.
+int make_tmap_2d(CUtensorMap* map, const void* base, bool f32, uint64_t rows, uint64_t cols,
+                 uint32_t box_cols, uint32_t box_rows);
 
-cudaError_t launch_gemm(int epilogue, const CUtensorMap* tmA, const CUtensorMap* tmB,
-                        const GemmArgs& args, int num_sms, cudaStream_t stream);
+// Tensor maps of one GEMM: A operand (box 64 x kGemmABoxRows), weights
+// (box 64 x kGemmBBoxRows) and the output (box 128 B x kGemmOutBoxRows; any
+// valid map for kEpiScorer, which writes through `out` directly).
+struct GemmMaps {
+  const CUtensorMap* a;
+  const CUtensorMap* b;
+  const CUtensorMap* out;
+};
+
+cudaError_t launch_gemm(int epilogue, const GemmMaps& maps, const GemmArgs& args, int num_sms,
+                        cudaStream_t stream);
 
 // ---- attention over compacted sequences ----------------------------------------
 struct AttnArgs {

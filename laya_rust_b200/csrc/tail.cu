@@ -8,8 +8,8 @@
 // (:453-465: the sequence's first row ++ features), act MLP
 // (graph.rs:171-176: W1 [256,1028] + b1, GELU, W2 [2,256] + b2).
 // The 1024 -> 1024 scorer hidden layer runs in the GEMM (kEpiScorer), which
-// leaves one partial dot product per 256-column tile; they are summed here in
-// a fixed order.
+// leaves one partial dot product per 128 output columns; they are summed here
+// in a fixed order.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -42,7 +42,7 @@ __global__ void __launch_bounds__(256) tail_kernel(const TailArgs a) {
     float v;
     if (a.mmask[r] != 0) {
       v = a.partial[r];
-      for (int nt = 1; nt < HID / 256; ++nt) v += a.partial[static_cast<size_t>(nt) * a.ldp + r];
+      for (int nt = 1; nt < kScorerPartials; ++nt) v += a.partial[static_cast<size_t>(nt) * a.ldp + r];
       v += a.score_bias;
     } else {
       v = -10000.0f;

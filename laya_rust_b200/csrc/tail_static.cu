@@ -15,7 +15,7 @@
 //
 // Limits and sharing:
 //   * at most kStaticMaxRows = n*k marker rows per call (larger calls are
-//     rejected with LAYA_E_INVALID); the array (4 MiB of rows + 32 KiB of
+//     rejected with LAYA_E_INVALID); the array (4 MiB of rows + 64 KiB of
 //     partial sums + an error word) stays allocated on every GPU that loads
 //     the library until the process exits;
 //   * every call on a device shares the one array and it keeps the previous
@@ -44,7 +44,7 @@ namespace {
 constexpr int kStaticMaxRows = LAYA_TAIL_STATIC_MAX_ROWS;
 constexpr int kHid = 1024;
 constexpr size_t kRowsBytes = static_cast<size_t>(kStaticMaxRows) * kHid * sizeof(__half);
-constexpr size_t kPartialBytes = static_cast<size_t>(kHid / kGemmBN) * kStaticMaxRows * sizeof(float);
+constexpr size_t kPartialBytes = static_cast<size_t>(kScorerPartials) * kStaticMaxRows * sizeof(float);
 constexpr size_t kScratchBytes = kRowsBytes + kPartialBytes + 256;
 
 // [rows f16 | partial f32 | error word]
@@ -76,7 +76,7 @@ int setup_device(int dev, DeviceState** out) {
       return LAYA_E_CUDA;
     }
     s.base = static_cast<unsigned char*>(p);
-    if (make_tmap_f16(&s.rows_map, s.base, kStaticMaxRows, kHid, kGemmBM) != 0) {
+    if (make_tmap_f16(&s.rows_map, s.base, kStaticMaxRows, kHid, kGemmABoxRows) != 0) {
       set_last_error("decision_tail_static: tensor map encode failed");
       return LAYA_E_CUDA;
     }
@@ -132,7 +132,9 @@ extern "C" int laya_decision_tail_static(laya_engine* e, const float* x, int n, 
   g.ldo = kStaticMaxRows;
   g.bias = w.hid_b;
   g.wvec = w.wout;
-  if ((ce = launch_gemm(kEpiScorer, &s->rows_map, w.hid_tmap, g, w.num_sms, st)) != cudaSuccess) return fail(ce);
+  if ((ce = launch_gemm(kEpiScorer, GemmMaps{&s->rows_map, w.hid_tmap, &s->rows_map}, g, w.num_sms, st)) !=
+      cudaSuccess)
+    return fail(ce);
   TailArgs t{};
   t.partial = partial;
   t.ldp = kStaticMaxRows;
