@@ -142,13 +142,20 @@ int laya_decision_tail_static(laya_engine *e, const float *x, int n, int k, cons
 
 /* ---- kernel self-tests (no counterpart in the reference) --------------------
  * Host in, host out; used by the GPU tests to check single kernels. */
-/* out[M,N] (f32) = A[M,K] . W[N,K]^T with A, W f16; N % 256 == 0, K % 64 == 0. */
+/* out[M,N] (f32) = A[M,K] . W[N,K]^T with A, W f16, on 256 x tile_n tiles
+ * (tile_n 256 or 128); N % tile_n == 0, K % 64 == 0. */
 int laya_selftest_gemm(int device, const uint16_t *a, const uint16_t *w, float *out, int m,
-                       int n, int k);
+                       int n, int k, int tile_n);
+/* Times the GEMM alone: random f16 operands on the device, `iters` launches
+ * of out[M,N] (f32) = A . W^T on 256 x tile_n tiles; *ms = mean device time
+ * per launch (CUDA events). */
+int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int iters, float *ms);
+
 /* Ragged attention on qkv [R,3072] f16 (q,k pre-scaled) for sequences packed
- * back to back with lengths lens[n]; window < 0 for global.  out [R,1024] f32. */
+ * back to back with lengths lens[n]; window < 0 for global.  out [R,1024] f32.
+ * impl 1: the tcgen05 kernel the forward uses; impl 0: the mma.sync kernel. */
 int laya_selftest_attention(int device, const uint16_t *qkv, const int32_t *lens, int n,
-                            int window, float *out);
+                            int window, float *out, int impl);
 
 #ifdef __cplusplus
 }

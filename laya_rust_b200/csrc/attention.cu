@@ -10,8 +10,12 @@
 //
 // Layout: qkv is token-major [R, 3072] (q | k | v, head h at columns h*64);
 // sequence b occupies rows [start[b], start[b] + len[b]).  The mask is a
-// predicate on (len, window): no mask tensor exists.  Key blocks that lie
-// entirely outside the +-64 band are never loaded.
+// predicate on (len, window): no mask tensor exists.  Work that the mask
+// removes is skipped, not computed: key blocks outside the CTA's band are
+// never loaded, a warp whose 16 query rows lie past the sequence end does no
+// math, and inside a key block each 16-key group that is past the end or
+// outside the warp's +-64 band skips its QK^T and PV MMAs (its scores would
+// be -inf and its probabilities 0, so the result is unchanged).
 //
 // CTA = 4 warps, 64 query rows (16 per warp) of one (sequence, head); keys in
 // blocks of 64 through a 2-deep cp.async ring in XOR-swizzled shared memory;
@@ -68,8 +72,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
 
 // Loads rows [row0, row0 + 64) of one 64-column slice of qkv into a swizzled
 // tile; rows at or past `limit` are zero-filled.
-__device__ __forceinline__ void load_tile(__half* tile, const __half* base, int row0, int limit,
-                                          int col) {
+__device__ __forceinline__ void load_tile(__half* tile, const __half* base, int row0, int limit, int col) {
   for (int i = threadIdx.x; i < 64 * 8; i += blockDim.x) {
     const int r = i >> 3, ch = i & 7;
     const bool ok = row0 + r < limit;
@@ -78,7 +81,7 @@ __device__ __forceinline__ void load_tile(__half* tile, const __half* base, int 
   }
 }
 
-__global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
+__global__ void __launch_bounds__(128, 4) attention_kernel(const AttnArgs a) {
   __shared__ __align__(128) __half sQ[QR * D];
   __shared__ __align__(128) __half sK[2][KR * D];
   __shared__ __align__(128) __half sV[2][KR * D];
@@ -89,9 +92,11 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   const __half* base = a.qkv + static_cast<size_t>(a.seq_start[b]) * LDQKV;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
+  const bool windowed = a.window >= 0;
 
+  // keys the whole CTA needs (union over its query rows)
   int k_lo = 0, k_hi = len;
-  if (a.window >= 0) {
+  if (windowed) {
     k_lo = q0 - a.window;
     if (k_lo < 0) k_lo = 0;
     const int q_last = (q0 + QR < len ? q0 + QR : len) - 1;
@@ -100,6 +105,17 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   }
   const int kb0 = k_lo / KR;
   const int kb1 = (k_hi + KR - 1) / KR;
+
+  // this warp's 16 query rows and the keys they can see
+  const int qw0 = q0 + warp * 16;
+  const bool warp_live = qw0 < len;
+  int wk_lo = 0, wk_hi = len;
+  if (windowed) {
+    wk_lo = qw0 - a.window;
+    if (wk_lo < 0) wk_lo = 0;
+    wk_hi = qw0 + 15 + a.window + 1;
+    if (wk_hi > len) wk_hi = len;
+  }
 
   load_tile(sQ, base, q0, len, h * D);
   load_tile(sK[0], base, kb0 * KR, len, 1024 + h * D);
@@ -112,7 +128,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.0f, 0.0f};
   uint32_t qf[4][4];
-  const int qi0 = q0 + warp * 16 + g;  // this thread's two query rows: qi0, qi0 + 8
+  const int qi0 = qw0 + g;  // this thread's two query rows: qi0, qi0 + 8
 
   for (int kb = kb0; kb < kb1; ++kb) {
     const int buf = (kb - kb0) & 1;
@@ -125,7 +141,125 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
       cp_wait<0>();
     }
     __syncthreads();
-    if (kb == kb0) {
+    const int key0 = kb * KR;
+    // 16-key groups of this block that hold at least one key this warp sees
+    bool live[4];
+#pragma unroll
+    for (int np = 0; np < 4; ++np) live[np] = warp_live && key0 + np * 16 < wk_hi && key0 + np * 16 + 16 > wk_lo;
+    if (live[0] || live[1] || live[2] || live[3]) {
+      if (kb == kb0) {
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int m = lane >> 3;
+          const int r = warp * 16 + (m & 1) * 8 + (lane & 7);
+          const int c = kk * 16 + (m >> 1) * 8;
+          ldsm_x4(qf[kk], sQ + swz(r, c));
+        }
+      }
+      // S = Q . K^T for this warp's 16 rows x 64 keys
+      float s[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
+      const __half* tk = sK[buf];
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        if (!live[np]) continue;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const int m = lane >> 3;
+          const int r = np * 16 + (m >> 1) * 8 + (lane & 7);
+          const int c = kk * 16 + (m & 1) * 8;
+          uint32_t kf[4];
+          ldsm_x4(kf, tk + swz(r, c));
+          mma16816(s[2 * np], qf[kk], kf[0], kf[1]);
+          mma16816(s[2 * np + 1], qf[kk], kf[2], kf[3]);
+        }
+      }
+      // mask (only where this block crosses the sequence end or a band edge
+      // of this warp's rows) + online softmax
+      bool need_mask = key0 + KR > len;
+      if (windowed) need_mask = need_mask || key0 < qw0 + 15 - a.window || key0 + KR - 1 > qw0 + a.window;
+      float mx[2] = {-INFINITY, -INFINITY};
+      if (need_mask) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kidx = key0 + nt * 8 + 2 * t + (e & 1);
+            const int qi = qi0 + (e >> 1) * 8;
+            bool ok = live[nt >> 1] && kidx < len;
+            if (windowed) {
+              const int d = qi - kidx;
+              ok = ok && d <= a.window && d >= -a.window;
+            }
+            const float v = ok ? s[nt][e] : -INFINITY;
+            s[nt][e] = v;
+            mx[e >> 1] = fmaxf(mx[e >> 1], v);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          mx[0] = fmaxf(mx[0], fmaxf(s[nt][0], s[nt][1]));
+          mx[1] = fmaxf(mx[1], fmaxf(s[nt][2], s[nt][3]));
+        }
+      }
+      float corr[2], m_use[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+        const float m_new = fmaxf(m_run[r], mx[r]);
+        m_use[r] = m_new == -INFINITY ? 0.0f : m_new;
+        corr[r] = exp2f((m_run[r] - m_use[r]) * L2E);
+        m_run[r] = m_new;
+      }
+      float rs[2] = {0.0f, 0.0f};
+      uint32_t pf[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float p0 = exp2f((s[nt][0] - m_use[0]) * L2E);
+        const float p1 = exp2f((s[nt][1] - m_use[0]) * L2E);
+        const float p2 = exp2f((s[nt][2] - m_use[1]) * L2E);
+        const float p3 = exp2f((s[nt][3] - m_use[1]) * L2E);
+        rs[0] += p0 + p1;
+        rs[1] += p2 + p3;
+        const int kk = nt >> 1;
+        if ((nt & 1) == 0) {
+          pf[kk][0] = pack2(p0, p1);
+          pf[kk][1] = pack2(p2, p3);
+        } else {
+          pf[kk][2] = pack2(p0, p1);
+          pf[kk][3] = pack2(p2, p3);
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) {
+        o[dt][0] *= corr[0];
+        o[dt][1] *= corr[0];
+        o[dt][2] *= corr[1];
+        o[dt][3] *= corr[1];
+      }
+      // O += P . V (16-key groups with no visible key have P = 0: skipped)
+      const __half* tv = sV[buf];
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (!live[kk]) continue;
+#pragma unroll
+        for (int dp = 0; dp < 4; ++dp) {
+          const int m = lane >> 3;
+          const int r = kk * 16 + (m & 1) * 8 + (lane & 7);
+          const int c = dp * 16 + (m >> 1) * 8;
+          uint32_t vf[4];
+          ldsm_x4_t(vf, tv + swz(r, c));
+          mma16816(o[2 * dp], pf[kk], vf[0], vf[1]);
+          mma16816(o[2 * dp + 1], pf[kk], vf[2], vf[3]);
+        }
+      }
+    } else if (kb == kb0 && warp_live) {
+      // keep the Q fragments for later blocks of this warp
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const int m = lane >> 3;
@@ -134,99 +268,10 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
         ldsm_x4(qf[kk], sQ + swz(r, c));
       }
     }
-    // S = Q . K^T for this warp's 16 rows x 64 keys
-    float s[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.0f;
-    const __half* tk = sK[buf];
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) {
-        const int m = lane >> 3;
-        const int r = np * 16 + (m >> 1) * 8 + (lane & 7);
-        const int c = kk * 16 + (m & 1) * 8;
-        uint32_t kf[4];
-        ldsm_x4(kf, tk + swz(r, c));
-        mma16816(s[2 * np], qf[kk], kf[0], kf[1]);
-        mma16816(s[2 * np + 1], qf[kk], kf[2], kf[3]);
-      }
-    }
-    // mask + online softmax
-    const int key0 = kb * KR;
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int kidx = key0 + nt * 8 + 2 * t + (e & 1);
-        const int qi = qi0 + (e >> 1) * 8;
-        bool ok = kidx < len;
-        if (a.window >= 0) {
-          const int d = qi - kidx;
-          ok = ok && d <= a.window && d >= -a.window;
-        }
-        const float v = ok ? s[nt][e] : -INFINITY;
-        s[nt][e] = v;
-        mx[e >> 1] = fmaxf(mx[e >> 1], v);
-      }
-    }
-    float corr[2], m_use[2];
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      m_use[r] = m_new == -INFINITY ? 0.0f : m_new;
-      corr[r] = exp2f((m_run[r] - m_use[r]) * L2E);
-      m_run[r] = m_new;
-    }
-    float rs[2] = {0.0f, 0.0f};
-    uint32_t pf[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float p0 = exp2f((s[nt][0] - m_use[0]) * L2E);
-      const float p1 = exp2f((s[nt][1] - m_use[0]) * L2E);
-      const float p2 = exp2f((s[nt][2] - m_use[1]) * L2E);
-      const float p3 = exp2f((s[nt][3] - m_use[1]) * L2E);
-      rs[0] += p0 + p1;
-      rs[1] += p2 + p3;
-      const int kk = nt >> 1;
-      if ((nt & 1) == 0) {
-        pf[kk][0] = pack2(p0, p1);
-        pf[kk][1] = pack2(p2, p3);
-      } else {
-        pf[kk][2] = pack2(p0, p1);
-        pf[kk][3] = pack2(p2, p3);
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
-#pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      o[dt][0] *= corr[0];
-      o[dt][1] *= corr[0];
-      o[dt][2] *= corr[1];
-      o[dt][3] *= corr[1];
-    }
-    // O += P . V
-    const __half* tv = sV[buf];
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-#pragma unroll
-      for (int dp = 0; dp < 4; ++dp) {
-        const int m = lane >> 3;
-        const int r = kk * 16 + (m & 1) * 8 + (lane & 7);
-        const int c = dp * 16 + (m >> 1) * 8;
-        uint32_t vf[4];
-        ldsm_x4_t(vf, tv + swz(r, c));
-        mma16816(o[2 * dp], pf[kk], vf[0], vf[1]);
-        mma16816(o[2 * dp + 1], pf[kk], vf[2], vf[3]);
-      }
-    }
     __syncthreads();
   }
 
+  if (!warp_live) return;
   float inv[2];
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
@@ -243,8 +288,7 @@ __global__ void __launch_bounds__(128) attention_kernel(const AttnArgs a) {
       __half* orow = out + static_cast<size_t>(qi) * 1024;
 #pragma unroll
       for (int dt = 0; dt < 8; ++dt)
-        *reinterpret_cast<uint32_t*>(orow + dt * 8 + 2 * t) =
-            pack2(o[dt][2 * r] * inv[r], o[dt][2 * r + 1] * inv[r]);
+        *reinterpret_cast<uint32_t*>(orow + dt * 8 + 2 * t) = pack2(o[dt][2 * r] * inv[r], o[dt][2 * r + 1] * inv[r]);
     }
   }
 }

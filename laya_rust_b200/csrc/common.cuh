@@ -21,6 +21,7 @@ enum DeviceError : int {
   kErrGemmMmaWait = 2,
   kErrGemmEpilogueWait = 3,
   kErrGemmTeardownWait = 4,
+  kErrAttnWait = 5,
 };
 
 // 2 s of wall clock: far above any legitimate wait in these kernels
@@ -88,6 +89,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 }
 
 // ---- TMA ----------------------------------------------------------------
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (TMA stores, tcgen05.mma operands).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }

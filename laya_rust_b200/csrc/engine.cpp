@@ -175,15 +175,18 @@ struct DevBuf {
 
 struct Weight {
   DevBuf buf;
-  CUtensorMap tmap;  // Linear weights only
+  CUtensorMap tmap;         // Linear weights only
+  CUtensorMap tmap_narrow;  // Linear weights with 1024 rows: box for 256 x 128 tiles
   std::vector<float> host;  // small tensors the host also needs (rope, scorer bias)
   bool present = false;
 };
 
 // Host-side plan of one request: validated and compacted (real tokens only).
 struct HostPlan {
-  int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
+  int n = 0, l = 0, k = 0, R = 0, nblocks = 0, nshort = 0;
   std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row;
+  // attention work: (sequence, first query row), kAttnTcQRows apart; the
+  // first nshort entries are sequences of at most kAttnTcQRows tokens
   std::vector<int2> blocks;
   std::vector<uint8_t> rowtype;
   std::vector<int8_t> mmask;
@@ -277,8 +280,12 @@ HostPlan make_plan(const laya_req* q) {
       p.pos[p.seq_start[b] + t] = t;
       p.rowtype[p.seq_start[b] + t] = (uint8_t)q->qtype[b];
     }
-    for (int q0 = 0; q0 < p.seq_len[b]; q0 += kAttnQRows) p.blocks.push_back(make_int2(b, q0));
+    if (p.seq_len[b] <= kAttnTcQRows) p.blocks.push_back(make_int2(b, 0));
   }
+  p.nshort = (int)p.blocks.size();
+  for (int b = 0; b < p.n; ++b)
+    if (p.seq_len[b] > kAttnTcQRows)
+      for (int q0 = 0; q0 < p.seq_len[b]; q0 += kAttnTcQRows) p.blocks.push_back(make_int2(b, q0));
   p.nblocks = (int)p.blocks.size();
   p.cls_row.resize(p.n);
   p.mk_row.resize((size_t)p.n * p.k);
@@ -310,6 +317,7 @@ HostPlan make_plan(const laya_req* q) {
 struct PlanMaps {
   CUtensorMap a_t16, a_ctx, a_gate, a_hmlp, a_mk;  // GEMM A operands
   CUtensorMap o_qkv, o_x, o_gate, o_hmlp;          // GEMM outputs
+  CUtensorMap qkv_tiles;                           // attention: 64-column x 128-row boxes of qkv
   uint64_t gen = ~0ull;                            // arena generation encoded for
 };
 
@@ -458,6 +466,8 @@ struct Engine {
           const uint64_t kdim = (uint64_t)role.shape[1];
           if (make_tmap_f16(&wt.tmap, wt.buf.p, rows, kdim, kGemmBBoxRows) != 0)
             throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
+          if (rows == (uint64_t)H && make_tmap_f16(&wt.tmap_narrow, wt.buf.p, rows, kdim, kGemmBBoxRowsNarrow) != 0)
+            throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
         }
         break;
       }
@@ -549,7 +559,8 @@ struct Engine {
         make_tmap_f16(&m.a_gate, gate.p, R, INTER, ab) || make_tmap_f16(&m.a_hmlp, hmlp.p, R, HEAD_INTER, ab) ||
         make_tmap_f16(&m.a_mk, mk16.p, nk, H, ab) || make_tmap_2d(&m.o_qkv, qkv.p, false, R, 3 * H, 64, ob) ||
         make_tmap_2d(&m.o_x, x.p, true, R, H, 32, ob) || make_tmap_2d(&m.o_gate, gate.p, false, R, INTER, 64, ob) ||
-        make_tmap_2d(&m.o_hmlp, hmlp.p, false, R, HEAD_INTER, 64, ob))
+        make_tmap_2d(&m.o_hmlp, hmlp.p, false, R, HEAD_INTER, 64, ob) ||
+        make_tmap_2d(&m.qkv_tiles, qkv.p, false, R, 3 * H, 64, kAttnTcQRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed for the arena");
     m.gen = arena_gen;
   }
@@ -561,9 +572,31 @@ struct Engine {
     a.N = N;
     a.K = K;
     a.err = err.as<int>();
-    ck(launch_gemm(epi, GemmMaps{&A, &Wt.tmap, &Out}, a, num_sms, stream), "gemm launch");
+    // 256 x 128 tiles (twice the tiles per wave for N = 1024) measured slower
+    // than 256 x 256 on the residual GEMMs: the smaller stages leave the TMA
+    // latency exposed.  They stay available through launch_gemm's `bn`.
+    const bool narrow = false;
+    ck(launch_gemm(epi, GemmMaps{&A, narrow ? &Wt.tmap_narrow : &Wt.tmap, &Out}, a, num_sms, stream,
+                   narrow ? kGemmBNNarrow : kGemmBN),
+       "gemm launch");
     ++nl;
     mark(kind);
+  }
+
+  // Attention over every sequence: one launch for sequences of at most 128
+  // tokens (single-pass kernel) and one for longer ones (two-pass kernel).
+  void attention(const PlanMaps& M, AttnArgs aa, const HostPlan& p, int64_t& nl) {
+    if (p.nshort > 0) {
+      ck(launch_attention_tc(&M.qkv_tiles, aa, p.nshort, true, err.as<int>(), stream), "attention");
+      ++nl;
+      mark(kProfAttn);
+    }
+    if (p.nblocks > p.nshort) {
+      aa.blocks += p.nshort;
+      ck(launch_attention_tc(&M.qkv_tiles, aa, p.nblocks - p.nshort, false, err.as<int>(), stream), "attention");
+      ++nl;
+      mark(kProfAttn);
+    }
   }
 
   // Enqueues one forward of plan `dp` on the stream (graph.rs:86-186).
@@ -603,9 +636,7 @@ struct Engine {
       gemm(kEpiQkvRope, M.a_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), M.o_qkv, R, 3 * H, H, g, nl,
            kProfQkv);
       aa.window = global ? -1 : WINDOW;
-      ck(launch_attention(aa, p.nblocks, stream), "attention");
-      ++nl;
-      mark(kProfAttn);
+      attention(M, aa, p, nl);
       GemmArgs r{};
       r.out = x.p;
       r.ldo = H;
@@ -649,9 +680,7 @@ struct Engine {
       g.scale = SCALE;
       gemm(kEpiQkvBias, M.a_t16, W(hn(hl, "self_attn.in_proj_weight")), M.o_qkv, R, 3 * H, H, g, nl, kProfHead);
       aa.window = -1;
-      ck(launch_attention(aa, p.nblocks, stream), "attention");
-      ++nl;
-      mark(kProfAttn);
+      attention(M, aa, p, nl);
       GemmArgs r{};
       r.out = x.p;
       r.ldo = H;
@@ -1122,9 +1151,12 @@ void laya_plan_destroy(laya_plan* p) { delete p; }
 
 void* laya_stream(laya_engine* e) { return e ? (void*)e->e->stream : nullptr; }
 
-int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float* out, int m, int n, int k) {
+int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float* out, int m, int n, int k,
+                       int tile_n) {
   return guard([&] {
-    if (!a || !wt || !out || m <= 0 || n <= 0 || k <= 0 || n % laya::kGemmBN || k % laya::kGemmBK)
+    if (tile_n != laya::kGemmBN && tile_n != laya::kGemmBNNarrow)
+      throw Error(LAYA_E_INVALID, "selftest_gemm: tile_n must be 256 or 128");
+    if (!a || !wt || !out || m <= 0 || n <= 0 || k <= 0 || n % tile_n || k % laya::kGemmBK)
       throw Error(LAYA_E_INVALID, "selftest_gemm: bad shape");
     laya::ck(cudaSetDevice(device), "cudaSetDevice");
     int sms = 0;
@@ -1141,7 +1173,7 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
     laya::ck(cudaMemcpy(dw.p, wt, (size_t)n * k * 2, cudaMemcpyHostToDevice), "h2d");
     CUtensorMap ta, tw, to;
     if (laya::make_tmap_f16(&ta, da.p, m, k, laya::kGemmABoxRows) ||
-        laya::make_tmap_f16(&tw, dw.p, n, k, laya::kGemmBBoxRows) ||
+        laya::make_tmap_f16(&tw, dw.p, n, k, tile_n / 2) ||
         laya::make_tmap_2d(&to, dout.p, true, m, n, 32, laya::kGemmOutBoxRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed");
     laya::GemmArgs g{};
@@ -1151,7 +1183,7 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
     g.err = derr.as<int>();
     g.out = dout.p;
     g.ldo = n;
-    laya::ck(laya::launch_gemm(laya::kEpiStoreF32, laya::GemmMaps{&ta, &tw, &to}, g, sms, 0), "gemm launch");
+    laya::ck(laya::launch_gemm(laya::kEpiStoreF32, laya::GemmMaps{&ta, &tw, &to}, g, sms, 0, tile_n), "gemm launch");
     laya::ck(cudaDeviceSynchronize(), "gemm run");
     int ev = 0;
     laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
@@ -1160,10 +1192,63 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
   });
 }
 
-int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens, int n, int window, float* out) {
+int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int iters, float* ms) {
   return guard([&] {
-    if (!qkv || !lens || !out || n <= 0) throw Error(LAYA_E_INVALID, "selftest_attention: bad argument");
+    if (!ms || m <= 0 || n <= 0 || k <= 0 || iters <= 0 || (tile_n != laya::kGemmBN && tile_n != laya::kGemmBNNarrow) ||
+        n % tile_n || k % laya::kGemmBK)
+      throw Error(LAYA_E_INVALID, "bench_gemm: bad shape");
     laya::ck(cudaSetDevice(device), "cudaSetDevice");
+    int sms = 0;
+    laya::ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "attr");
+    laya::DevBuf da, dw, dout, derr;
+    da.alloc((size_t)m * k * 2, "a");
+    dw.alloc((size_t)n * k * 2, "w");
+    dout.alloc((size_t)m * n * 4, "out");
+    derr.alloc(256, "err");
+    // operands: a fixed small-integer pattern (exact in f16), no host copies
+    laya::ck(cudaMemset(da.p, 0x3c, da.bytes), "memset");
+    laya::ck(cudaMemset(dw.p, 0x2c, dw.bytes), "memset");
+    laya::ck(cudaMemset(derr.p, 0, 256), "memset");
+    CUtensorMap ta, tw, to;
+    if (laya::make_tmap_f16(&ta, da.p, m, k, laya::kGemmABoxRows) || laya::make_tmap_f16(&tw, dw.p, n, k, tile_n / 2) ||
+        laya::make_tmap_2d(&to, dout.p, true, m, n, 32, laya::kGemmOutBoxRows))
+      throw Error(LAYA_E_CUDA, "tensor map encode failed");
+    laya::GemmArgs g{};
+    g.M = m;
+    g.N = n;
+    g.K = k;
+    g.err = derr.as<int>();
+    g.out = dout.p;
+    g.ldo = n;
+    const laya::GemmMaps maps{&ta, &tw, &to};
+    for (int i = 0; i < 3; ++i)
+      laya::ck(laya::launch_gemm(laya::kEpiStoreF32, maps, g, sms, 0, tile_n), "gemm launch");
+    cudaEvent_t e0, e1;
+    laya::ck(cudaEventCreate(&e0), "event");
+    laya::ck(cudaEventCreate(&e1), "event");
+    laya::ck(cudaEventRecord(e0, 0), "event");
+    for (int i = 0; i < iters; ++i)
+      laya::ck(laya::launch_gemm(laya::kEpiStoreF32, maps, g, sms, 0, tile_n), "gemm launch");
+    laya::ck(cudaEventRecord(e1, 0), "event");
+    laya::ck(cudaEventSynchronize(e1), "sync");
+    float t = 0;
+    laya::ck(cudaEventElapsedTime(&t, e0, e1), "elapsed");
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    int ev = 0;
+    laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
+    if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("gemm device wait expired (code %d)", ev));
+    *ms = t / iters;
+  });
+}
+
+int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens, int n, int window, float* out,
+                            int impl) {
+  return guard([&] {
+    if (!qkv || !lens || !out || n <= 0 || (impl != 0 && impl != 1))
+      throw Error(LAYA_E_INVALID, "selftest_attention: bad argument");
+    laya::ck(cudaSetDevice(device), "cudaSetDevice");
+    const int qrows = impl == 1 ? laya::kAttnTcQRows : laya::kAttnQRows;
     std::vector<int> start(n), len(n);
     std::vector<int2> blocks;
     int R = 0;
@@ -1171,10 +1256,18 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
       if (lens[b] <= 0) throw Error(LAYA_E_INVALID, "selftest_attention: empty sequence");
       start[b] = R;
       len[b] = lens[b];
-      for (int q0 = 0; q0 < lens[b]; q0 += laya::kAttnQRows) blocks.push_back(make_int2(b, q0));
       R += lens[b];
     }
-    laya::DevBuf dq, dout, ds, dl, db;
+    // tcgen05: short sequences first (one block each), then the long ones
+    int nshort = 0;
+    if (impl == 1)
+      for (int b = 0; b < n; ++b)
+        if (len[b] <= qrows) blocks.push_back(make_int2(b, 0));
+    nshort = (int)blocks.size();
+    for (int b = 0; b < n; ++b)
+      if (impl == 0 || len[b] > qrows)
+        for (int q0 = 0; q0 < len[b]; q0 += qrows) blocks.push_back(make_int2(b, q0));
+    laya::DevBuf dq, dout, ds, dl, db, derr;
     dq.alloc((size_t)R * 3072 * 2, "qkv");
     dout.alloc((size_t)R * 1024 * 2, "out");
     ds.alloc(n * 4, "start");
@@ -1185,8 +1278,25 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
     laya::ck(cudaMemcpy(dl.p, len.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(db.p, blocks.data(), blocks.size() * sizeof(int2), cudaMemcpyHostToDevice), "h2d");
     laya::AttnArgs a{dq.as<__half>(), dout.as<__half>(), ds.as<int>(), dl.as<int>(), db.as<int2>(), window};
-    laya::ck(laya::launch_attention(a, (int)blocks.size(), 0), "attention launch");
-    laya::ck(cudaDeviceSynchronize(), "attention run");
+    if (impl == 1) {
+      derr.alloc(256, "err");
+      laya::ck(cudaMemset(derr.p, 0, 256), "memset");
+      CUtensorMap tm;
+      if (laya::make_tmap_2d(&tm, dq.p, false, R, 3072, 64, laya::kAttnTcQRows))
+        throw Error(LAYA_E_CUDA, "tensor map encode failed");
+      laya::ck(laya::launch_attention_tc(&tm, a, nshort, true, derr.as<int>(), 0), "attention launch");
+      laya::AttnArgs al = a;
+      al.blocks += nshort;
+      laya::ck(laya::launch_attention_tc(&tm, al, (int)blocks.size() - nshort, false, derr.as<int>(), 0),
+               "attention launch");
+      laya::ck(cudaDeviceSynchronize(), "attention run");
+      int ev = 0;
+      laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
+      if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("attention device wait expired (code %d)", ev));
+    } else {
+      laya::ck(laya::launch_attention(a, (int)blocks.size(), 0), "attention launch");
+      laya::ck(cudaDeviceSynchronize(), "attention run");
+    }
     std::vector<uint16_t> h((size_t)R * 1024);
     laya::ck(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost), "d2h");
     for (size_t i = 0; i < h.size(); ++i) out[i] = laya::h2f_bits(h[i]);

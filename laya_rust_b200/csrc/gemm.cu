@@ -536,8 +536,16 @@ cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cud
 
 }  // namespace
 
-cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream) {
-  if (args.N % kGemmBN || args.K % BK || args.M < 0 || !m.a || !m.b || !m.out) return cudaErrorInvalidValue;
+cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, int num_sms, cudaStream_t stream,
+                        int bn) {
+  if (bn != kGemmBN && bn != kGemmBNNarrow) return cudaErrorInvalidValue;
+  if (args.N % bn || args.K % BK || args.M < 0 || !m.a || !m.b || !m.out) return cudaErrorInvalidValue;
+  if (bn == kGemmBNNarrow) {
+    // narrow tiles: the residual GEMMs with N = 1024 (more tiles per wave)
+    if (epilogue == kEpiResid) return launch_one<kEpiResid, kGemmBNNarrow>(m, args, num_sms, stream);
+    if (epilogue == kEpiStoreF32) return launch_one<kEpiStoreF32, kGemmBNNarrow>(m, args, num_sms, stream);
+    return cudaErrorInvalidValue;
+  }
   switch (epilogue) {
     case kEpiQkvRope: return launch_one<kEpiQkvRope, kGemmBN>(m, args, num_sms, stream);
     case kEpiQkvBias: return launch_one<kEpiQkvBias, kGemmBN>(m, args, num_sms, stream);

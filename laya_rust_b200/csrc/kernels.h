@@ -15,6 +15,9 @@ constexpr int kGemmBN = 256;
 constexpr int kGemmBK = 64;
 constexpr int kGemmABoxRows = 128;
 constexpr int kGemmBBoxRows = kGemmBN / 2;
+// Narrow 256 x 128 tiles for N = 1024 outputs: twice the tiles per wave.
+constexpr int kGemmBNNarrow = 128;
+constexpr int kGemmBBoxRowsNarrow = kGemmBNNarrow / 2;
 // Output tiles leave through 32-row TMA boxes of 128 bytes per row:
 // 64 f16 columns or 32 f32 columns.
 constexpr int kGemmOutBoxRows = 32;
@@ -66,8 +69,10 @@ struct GemmMaps {
   const CUtensorMap* out;
 };
 
+// bn: kGemmBN, or kGemmBNNarrow for kEpiResid / kEpiStoreF32 (then the
+// weight map's box has kGemmBNNarrow / 2 rows).
 cudaError_t launch_gemm(int epilogue, const GemmMaps& maps, const GemmArgs& args, int num_sms,
-                        cudaStream_t stream);
+                        cudaStream_t stream, int bn = kGemmBN);
 
 // ---- attention over compacted sequences ----------------------------------------
 struct AttnArgs {
@@ -80,6 +85,13 @@ struct AttnArgs {
 };
 cudaError_t launch_attention(const AttnArgs& a, int num_blocks, cudaStream_t stream);
 constexpr int kAttnQRows = 64;
+// tcgen05 attention: blocks of kAttnTcQRows query rows; tm_qkv maps the qkv
+// buffer ([R, 3072] f16, box 64 columns x 128 rows, 128-byte swizzle).
+// short_seqs: every block's sequence has at most kAttnTcQRows tokens (one key
+// block, single pass, four CTAs per SM); otherwise the two-pass kernel.
+constexpr int kAttnTcQRows = 128;
+cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_blocks, bool short_seqs,
+                                int* err, cudaStream_t stream);
 
 // ---- row kernels -----------------------------------------------------------------
 // x[r] = t[r] = LN(emb[tok[r]]) * w ; writes f32 residual and f16 copy

@@ -73,9 +73,9 @@ def lib():
         L.laya_stream.restype = vp
         L.laya_decision_tail_static.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp]
         L.laya_selftest_gemm.argtypes = [ctypes.c_int, vp, vp, _f32p, ctypes.c_int, ctypes.c_int,
-                                         ctypes.c_int]
+                                         ctypes.c_int, ctypes.c_int]
         L.laya_selftest_attention.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_int32),
-                                              ctypes.c_int, ctypes.c_int, _f32p]
+                                              ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -248,23 +248,26 @@ class Engine:
         self.close()
 
 
-def selftest_gemm(a: np.ndarray, w: np.ndarray, device: int = 0) -> np.ndarray:
-    """out = a . w^T through the tcgen05 GEMM (f16 inputs, f32 result)."""
+def selftest_gemm(a: np.ndarray, w: np.ndarray, device: int = 0, tile_n: int = 256) -> np.ndarray:
+    """out = a . w^T through the tcgen05 GEMM (f16 inputs, f32 result) on
+    256 x tile_n tiles."""
     a = np.ascontiguousarray(a, dtype=np.float16)
     w = np.ascontiguousarray(w, dtype=np.float16)
     m, k = a.shape
     n = w.shape[0]
     out = np.empty((m, n), np.float32)
-    _check(lib().laya_selftest_gemm(device, a.ctypes.data, w.ctypes.data, out.ctypes.data_as(_f32p), m, n, k))
+    _check(lib().laya_selftest_gemm(device, a.ctypes.data, w.ctypes.data, out.ctypes.data_as(_f32p), m, n, k,
+                                    tile_n))
     return out
 
 
-def selftest_attention(qkv: np.ndarray, lens, window: int, device: int = 0) -> np.ndarray:
-    """Ragged attention kernel on packed qkv [R, 3072] f16; returns [R, 1024] f32."""
+def selftest_attention(qkv: np.ndarray, lens, window: int, device: int = 0, impl: int = 1) -> np.ndarray:
+    """Ragged attention on packed qkv [R, 3072] f16; returns [R, 1024] f32.
+    impl 1: the tcgen05 kernel the forward uses; impl 0: the mma.sync kernel."""
     qkv = np.ascontiguousarray(qkv, dtype=np.float16)
     lens = np.ascontiguousarray(lens, dtype=np.int32)
     out = np.empty((qkv.shape[0], 1024), np.float32)
     _check(lib().laya_selftest_attention(device, qkv.ctypes.data,
                                          lens.ctypes.data_as(ctypes.POINTER(ctypes.c_int32)),
-                                         len(lens), window, out.ctypes.data_as(_f32p)))
+                                         len(lens), window, out.ctypes.data_as(_f32p), impl))
     return out

@@ -13,13 +13,14 @@ from laya_rust_b200 import engine as E
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (200, 256, 64), (129, 3072, 1024), (1000, 512, 1024),
-                                   (300, 1024, 2624), (2048, 1024, 4096)])
-def test_gemm_matches_torch_fp32(m, n, k):
+@pytest.mark.parametrize("m,n,k,tile_n", [(1, 256, 64, 256), (200, 256, 64, 256), (129, 3072, 1024, 256),
+                                          (1000, 512, 1024, 256), (300, 1024, 2624, 256), (2048, 1024, 4096, 256),
+                                          (1, 128, 64, 128), (9872, 1024, 1024, 128), (777, 1024, 2624, 128)])
+def test_gemm_matches_torch_fp32(m, n, k, tile_n):
     rng = np.random.default_rng(m * 7 + n + k)
     a = rng.standard_normal((m, k)).astype(np.float16)
     w = (rng.standard_normal((n, k)) * 0.05).astype(np.float16)
-    got = E.selftest_gemm(a, w)
+    got = E.selftest_gemm(a, w, tile_n=tile_n)
     ref = (torch.from_numpy(a).float() @ torch.from_numpy(w).float().T).numpy()
     err = np.abs(got - ref).max()
     scale = np.abs(ref).max()
@@ -46,13 +47,14 @@ def attention_ref(qkv, lens, window):
     return out.numpy()
 
 
+@pytest.mark.parametrize("impl", [1, 0], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("window", [-1, 64])
-def test_attention_matches_torch_fp32(window):
+def test_attention_matches_torch_fp32(window, impl):
     rng = np.random.default_rng(5 + window)
-    lens = [1, 17, 64, 65, 128, 129, 200, 512]
+    lens = [1, 17, 64, 65, 128, 129, 200, 256, 300, 512]
     R = sum(lens)
     qkv = (rng.standard_normal((R, 3072)) * 0.7).astype(np.float16)
-    got = E.selftest_attention(qkv, lens, window)
+    got = E.selftest_attention(qkv, lens, window, impl=impl)
     ref = attention_ref(qkv, lens, window)
     err = np.abs(got - ref).max()
     # P and the output are rounded to f16 (rel 2^-11); values are O(1)
