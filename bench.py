@@ -1,23 +1,39 @@
 #!/usr/bin/env python
 """Benchmark of the laya encoder forward on B200.
 
-Metric: encoder tokens/s, reported on REAL tokens (padding is
-never computed; padded tokens/s is reported beside it).  A step is one forward
-of the workload.  The default workload is the --max-tokens 16384 budget
-(configuration 2: 128 sequences x 128 padded tokens, real lengths U[24,128]).
+Metric: encoder tokens/s, counted on REAL tokens (padding is
+never computed; padded tokens/s is reported beside it), plus request latency.
+Workloads (--config), all seeded synthetic data on a random-init f16 model:
 
-  value     device-resident: the request is uploaded once (a plan) and each
-            step replays the forward's CUDA graph; CUDA events on the engine
-            stream around K steps, max over ranks.
+  forward-16k  config 2 (default): the --max-tokens 16384 budget, 128
+               sequences x 128 padded tokens, real lengths U[24,128].  A step
+               is one forward.
+  long-state   config 3: 8 sequences x 512 tokens.  A step is one forward.
+  layer        config 1: one encoder layer alone on 32 sequences padded to
+               256 (real lengths U[16,256]), f16 N(0,1) activations; global
+               layer 3 and local layer 1 timed separately, L2 flushed before
+               every step (the layer's weights and activations fit in L2).
+  request      config 0: one System One request (48-word state, a choice
+               question with 2 criteria, a noul question) through the request
+               path (group_by_budget, build_batch, forward, scoring); the
+               metric is its latency (ms, p50 over the steps).
+  stream       config 4: 4096 seeded requests dealt round-robin to the GPUs;
+               each GPU packs its share into <=16384-token forwards.  Steps are
+               the forwards of one pass over the stream.
+
+  value     device-resident: requests uploaded once (plans), forwards
+            enqueued back to back (CUDA graph replay where one plan repeats);
+            CUDA events on the engine stream, max over ranks.
   e2e       through the public call (Engine.forward -> laya_forward): host
             index arrays in, host logits/act out, every step; wall clock
-            around K calls after a barrier, max over ranks.
+            after a barrier, max over ranks.
   roofline  the dominant kernel family (the tcgen05 GEMM, all its launches):
             algorithmic real-token FLOPs / device time from CUDA events
             recorded after every launch over K more steps.
 
-N GPUs (torchrun): one engine per GPU, each rank runs its own seeded batch
-(seed = rank), no collective on the data path; weak scaling.
+N GPUs (torchrun): one engine per GPU, each rank works on its own requests,
+no collective on the data path (NCCL only for the barrier and the final
+reductions); weak scaling.
 
 --impl reference: the reference's CPU algorithm (the C restatement in
 oracle/, the Rust reference cannot be built here) on a bounded sample of the
@@ -27,6 +43,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -39,6 +56,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "encoder tokens/sec"
 UNIT = "real tokens/s"
+LAT_METRIC = "request latency p50"
+CONFIGS = ["forward-16k", "long-state", "layer", "request", "stream"]
+DATA = "synthetic (seeded ids, random-init weights)"
+MODEL = "laya (ModernBERT-large 28L + 2L head), random-init f16 GGUF seed 0"
+LAYERS = (("global", 3), ("local", 1))
 
 
 def parse():
@@ -47,8 +69,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--config", default="forward-16k", choices=["forward-16k", "long-state"])
+    ap.add_argument("--config", default="forward-16k", choices=CONFIGS)
     ap.add_argument("--cpu-sample", type=int, default=4, help="sequences in the CPU baseline sample")
+    ap.add_argument("--requests", type=int, default=4096, help="requests in the stream configuration")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -58,14 +81,34 @@ def env_rank():
             int(os.environ.get("WORLD_SIZE", 1)))
 
 
+def pct(sorted_vals, p):
+    """main.rs:559-565: element round(p/100 * (n-1)) of the sorted sample."""
+    if not sorted_vals:
+        return 0.0
+    i = int(math.floor(p / 100.0 * (len(sorted_vals) - 1) + 0.5))
+    return sorted_vals[min(i, len(sorted_vals) - 1)]
+
+
+def latency_summary(ms):
+    s = sorted(ms)
+    return {"min": s[0], "p50": pct(s, 50), "p90": pct(s, 90), "p99": pct(s, 99), "max": s[-1],
+            "mean": sum(s) / len(s), "count": len(s)}
+
+
 def workload(name, seed):
     from laya_rust_b200 import workloads
-    return workloads.forward_16k(seed) if name == "forward-16k" else workloads.long_state(seed + 3)
+    if name == "forward-16k":
+        return workloads.forward_16k(seed)
+    if name == "long-state":
+        return workloads.long_state(seed + 3)
+    if name == "layer":
+        return workloads.layer_batch(seed + 1)
+    raise ValueError(name)
 
 
 def config_of(args, req, n):
     from laya_rust_b200 import workloads
-    return {"workload": args.config, "model": "laya (ModernBERT-large 28L + 2L head), random-init f16 GGUF seed 0",
+    return {"workload": args.config, "model": MODEL,
             "global_batch": req.n * n, "seq_len": req.l, "k_markers": req.k,
             "real_tokens_per_forward": workloads.real_tokens(req),
             "padded_tokens_per_forward": workloads.padded_tokens(req),
@@ -79,11 +122,36 @@ def sub_request(req, m):
                req.mmask.reshape(n, k)[:m], req.qtype[:m])
 
 
-def cpu_run(req, steps, warmup):
-    """Times the oracle (the reference CPU algorithm) on `req`; returns seconds per step."""
+def cpu_threads():
+    v = os.environ.get("LAYA_CPU_THREADS")
+    return int(v) if v and int(v) > 0 else os.cpu_count()
+
+
+def oracle_model():
     from laya_rust_b200 import modelgen
     from oracle.oracle import OracleModel
-    m = OracleModel(modelgen.cached_model(seed=0))
+    return OracleModel(modelgen.cached_model(seed=0))
+
+
+class OracleEngine:
+    """The oracle behind the Engine.forward call, so the request path
+    (batching.run_all) can run on the reference CPU algorithm."""
+
+    def __init__(self):
+        self.m = oracle_model()
+
+    def forward(self, req):
+        from laya_rust_b200.engine import Out
+        lg, act = self.m.forward(req.n, req.l, req.k, req.ids, req.att, req.mpos, req.mmask, req.qtype)
+        return Out(req.n, req.k, lg, act)
+
+    def close(self):
+        self.m.close()
+
+
+def cpu_run(req, steps, warmup):
+    """Times the oracle (the reference CPU algorithm) on `req`; returns seconds per step."""
+    m = oracle_model()
     times = []
     for i in range(warmup + steps):
         t0 = time.perf_counter()
@@ -94,9 +162,41 @@ def cpu_run(req, steps, warmup):
     return statistics.mean(times)
 
 
-def cpu_threads():
-    v = os.environ.get("LAYA_CPU_THREADS")
-    return int(v) if v and int(v) > 0 else os.cpu_count()
+def cpu_layer_run(req, steps, warmup):
+    """Times the oracle's one-layer call (global then local layer) on `req`;
+    returns seconds per layer."""
+    import numpy as np
+    m = oracle_model()
+    x = np.random.default_rng(1).standard_normal((req.n * req.l, 1024)).astype(np.float16).astype(np.float32)
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        for _, layer in LAYERS:
+            m.encoder_layer(req.n, req.l, req.att, layer, x)
+        if i >= warmup:
+            times.append((time.perf_counter() - t0) / len(LAYERS))
+    m.close()
+    return statistics.mean(times)
+
+
+def cpu_request_run(items, steps, warmup):
+    """Times the request path on the oracle; returns per-run milliseconds."""
+    from laya_rust_b200 import batching
+    eng = OracleEngine()
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        batching.run_all(eng, items)
+        if i >= warmup:
+            times.append((time.perf_counter() - t0) * 1e3)
+    eng.close()
+    return times
+
+
+def stream_sample():
+    """The CPU sample of the stream: the first 4 questions of request 0."""
+    from laya_rust_b200 import workloads
+    return workloads.request_stream(1, 4)[0][:4]
 
 
 class ClockSampler:
@@ -147,79 +247,136 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def base_line(args, metric, value, unit, n, ms_per_step, config, hib=True, **extra):
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": n, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": hib, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 operands, f32 accumulate", "data": DATA, "config": config}
+    line.update(extra)
+    return line
+
+
+# ---- reference arm -------------------------------------------------------------------
+
 def run_reference(args):
     rank, _, world = env_rank()
     if rank != 0:
         return
-    req = workload(args.config, 0)
-    sample = sub_request(req, args.cpu_sample)
     from laya_rust_b200 import workloads
-    real = workloads.real_tokens(sample)
-    sec = cpu_run(sample, args.steps, args.warmup)
-    v = real / sec
     cores = cpu_threads()
-    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded ids, random-init weights)",
-            "impl": "reference", "config": config_of(args, req, args.gpus),
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"first {args.cpu_sample} sequences of the {args.config} batch "
-                                       f"({real} real / {sample.n * sample.l} padded tokens) per step; "
-                                       "C restatement of the reference CPU backend (Rust reference not "
-                                       "buildable: no cargo in the image)"},
-            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    note = "C restatement of the reference CPU backend (Rust reference not buildable: no cargo in the image)"
+    if args.config in ("forward-16k", "long-state", "layer"):
+        req = workload(args.config, 0)
+        sample = sub_request(req, args.cpu_sample if args.config != "layer" else 2 * args.cpu_sample)
+        real = workloads.real_tokens(sample)
+        if args.config == "layer":
+            sec = cpu_layer_run(sample, args.steps, args.warmup)
+            what = "one encoder layer (global layer 3 and local layer 1 alternately)"
+        else:
+            sec = cpu_run(sample, args.steps, args.warmup)
+            what = "one forward"
+        v = real / sec
+        cfg = config_of(args, req, args.gpus)
+        sample_txt = (f"first {sample.n} sequences of the {args.config} batch ({real} real / "
+                      f"{sample.n * sample.l} padded tokens), {what} per step; {note}")
+        line = base_line(args, METRIC, v, UNIT, args.gpus, sec * 1e3, cfg, dtype="f32", impl="reference")
+    else:
+        items = workloads.single_request(0) if args.config == "request" else stream_sample()
+        times = cpu_request_run(items, args.steps, args.warmup)
+        lat = latency_summary(times)
+        toks = sum(len(i.seq) for i in items)
+        if args.config == "request":
+            v, unit, metric, hib = lat["p50"], "ms", LAT_METRIC, False
+        else:
+            v, unit, metric, hib = toks / (lat["mean"] / 1e3), UNIT, METRIC, True
+        cfg = {"workload": args.config, "model": MODEL, "questions": len(items), "real_tokens": toks}
+        sample_txt = (f"{'the request' if args.config == 'request' else 'first 4 questions of request 0'} "
+                      f"({len(items)} questions, {toks} tokens) through run_all per step; {note}")
+        line = base_line(args, metric, v, unit, args.gpus, lat["mean"], cfg, hib=hib, dtype="f32",
+                         impl="reference", latency_ms=lat)
+    line["cpu_baseline"] = {"value": line["value"], "unit": line["unit"], "cores": cores, "kind": "port",
+                            "sample": sample_txt}
+    line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     print(json.dumps(line), flush=True)
 
 
-def run_b200(args):
-    import numpy as np
-    import torch
-    import torch.distributed as dist
+# ---- B200 arm ------------------------------------------------------------------------
 
-    from laya_rust_b200 import modelgen, workloads
+class Dist:
+    def __init__(self):
+        import torch
+        self.torch = torch
+        self.rank, self.local, self.world = env_rank()
+        if self.world > 1:
+            import torch.distributed as dist
+            from datetime import timedelta
+            torch.cuda.set_device(self.local)
+            dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+        torch.cuda.set_device(self.local)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def _reduce(self, x, op):
+        if self.world == 1:
+            return x
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    def allmax(self, x):
+        return self._reduce(x, self.dist.ReduceOp.MAX if self.world > 1 else None)
+
+    def allsum(self, x):
+        return self._reduce(x, self.dist.ReduceOp.SUM if self.world > 1 else None)
+
+    def gather(self, obj):
+        if self.world == 1:
+            return [obj]
+        out = [None] * self.world
+        self.dist.all_gather_object(out, obj)
+        return out
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def open_engine(d):
+    from laya_rust_b200 import modelgen
     from laya_rust_b200.engine import Engine
+    if d.rank == 0:
+        modelgen.cached_model(seed=0)
+    d.barrier()
+    return Engine(modelgen.cached_model(seed=0), device=d.local)
 
-    rank, local, world = env_rank()
-    if world > 1:
-        from datetime import timedelta
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-    torch.cuda.set_device(local)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
+def ext_stream(d, eng):
+    return d.torch.cuda.ExternalStream(eng.stream(), device=d.torch.device("cuda", d.local))
 
-    def allmax(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
-    def allsum(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+def cpu_baseline_line(value, unit, sample):
+    return {"value": value, "unit": unit, "cores": cpu_threads(), "kind": "port", "sample": sample}
 
-    if rank == 0:
-        path = modelgen.cached_model(seed=0)
-    barrier()
-    path = modelgen.cached_model(seed=0)
-    eng = Engine(path, device=local)
-    req = workload(args.config, rank)
+
+def run_forward(args, d, eng):
+    """forward-16k / long-state: one forward of a fixed batch per step."""
+    import numpy as np
+    from laya_rust_b200 import workloads
+    torch = d.torch
+    req = workload(args.config, d.rank)
     plan = eng.plan(req)
     plan.capture()
     real, launches, upload = plan.stats()
-    stream = torch.cuda.ExternalStream(eng.stream(), device=torch.device("cuda", local))
+    stream = ext_stream(d, eng)
 
     for _ in range(args.warmup):
         plan.run()
     torch.cuda.synchronize()
-    clocks = ClockSampler(list(range(world))) if rank == 0 else None
-    barrier()
+    clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
+    d.barrier()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -228,15 +385,15 @@ def run_b200(args):
         plan.run()
     t1.record(stream)
     torch.cuda.synchronize()
-    barrier()
+    d.barrier()
     ms = t0.elapsed_time(t1)
-    ms_max = allmax(ms)
+    ms_max = d.allmax(ms)
     clk = clocks.stop() if clocks else None
     out = plan.outputs()
     assert np.all(np.isfinite(out.logits)) and np.all(np.isfinite(out.act))
 
-    total_real = allsum(real) * args.steps
-    total_padded = allsum(req.n * req.l) * args.steps
+    total_real = d.allsum(real) * args.steps
+    total_padded = d.allsum(req.n * req.l) * args.steps
     value = total_real / (ms_max / 1e3)
 
     # roofline of the dominant kernel family from per-launch events
@@ -256,43 +413,325 @@ def run_b200(args):
     # e2e through the public call: host arrays in, host logits/act out
     for _ in range(2):
         eng.forward(req)
-    barrier()
-    e0 = time.perf_counter()
+    d.barrier()
+    e_ms = []
     for _ in range(args.steps):
+        e0 = time.perf_counter()
         eng.forward(req)
-    e_sec = allmax(time.perf_counter() - e0)
-    barrier()
+        e_ms.append((time.perf_counter() - e0) * 1e3)
+    e_sec = d.allmax(sum(e_ms) / 1e3)
+    d.barrier()
     e2e = {"value": total_real / e_sec, "unit": UNIT, "h2d_bytes_per_step": upload,
            "d2h_bytes_per_step": 4 * (req.n * req.k + 2 * req.n), "ms_per_step": e_sec * 1e3 / args.steps,
+           "latency_ms": latency_summary(e_ms),
            "path": "laya_forward (validate + compact on host, one pinned H2D, graph-free launch, D2H)"}
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         sample = sub_request(req, args.cpu_sample)
         sec = cpu_run(sample, 1, 0)
-        cpu = {"value": workloads.real_tokens(sample) / sec, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"first {args.cpu_sample} sequences of the batch ({workloads.real_tokens(sample)} real / "
-                         f"{sample.n * sample.l} padded tokens), one forward"}
+        cpu = cpu_baseline_line(workloads.real_tokens(sample) / sec, UNIT,
+                                f"first {args.cpu_sample} sequences of the batch ({workloads.real_tokens(sample)} "
+                                f"real / {sample.n * sample.l} padded tokens), one forward")
 
-    if rank == 0:
-        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "f16 operands, f32 accumulate",
-                "data": "synthetic (seeded ids, random-init weights)",
-                "padded_tokens_per_s": total_padded / (ms_max / 1e3),
-                "config": config_of(args, req, world),
-                "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all launches)",
-                             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                             "peak_source": f"{pk_src} bf16_tflops_sustained", "traffic": None,
-                             "launches_per_step": gemm_launches // args.steps,
-                             "flops_per_step": workloads.gemm_flops(req)},
-                "kernels": kernels, "e2e": e2e, "gpu_launches": launches * args.steps,
-                "clocks": clk, "cpu_baseline": cpu}
+    if d.rank == 0:
+        line = base_line(args, METRIC, value, UNIT, d.world, ms_max / args.steps, config_of(args, req, d.world),
+                         padded_tokens_per_s=total_padded / (ms_max / 1e3),
+                         roofline={"bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all launches)",
+                                   "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                                   "peak_source": f"{pk_src} bf16_tflops_sustained", "traffic": None,
+                                   "launches_per_step": gemm_launches // args.steps,
+                                   "flops_per_step": workloads.gemm_flops(req)},
+                         kernels=kernels, e2e=e2e, gpu_launches=launches * args.steps, clocks=clk,
+                         cpu_baseline=cpu)
         print(json.dumps(line), flush=True)
     plan.close()
-    eng.close()
-    if world > 1:
-        dist.destroy_process_group()
+
+
+def layer_launches(req):
+    """Kernels laya_plan_run_layer enqueues: two row norms, four GEMMs and one
+    attention launch per kind of block present (sequences of at most 128
+    tokens run the single-pass kernel, longer ones the two-pass kernel)."""
+    lens = (req.att.reshape(req.n, req.l) != 0).sum(1)
+    return 6 + int((lens <= 128).any()) + int((lens > 128).any())
+
+
+def layer_flops(req, global_layer):
+    import numpy as np
+    lens = (req.att.reshape(req.n, req.l) != 0).sum(1).astype(np.float64)
+    real = float(lens.sum())
+    gemm = 2.0 * real * (1024 * 3072 + 1024 * 1024 + 1024 * 5248 + 2624 * 1024)
+    if global_layer:
+        pairs = float((lens ** 2).sum())
+    else:
+        pairs = 0.0
+        for r in lens.astype(np.int64):
+            i = np.arange(r)
+            pairs += float((np.minimum(i + 64, r - 1) - np.maximum(i - 64, 0) + 1).sum())
+    return gemm, 4.0 * 1024 * pairs
+
+
+def run_layer(args, d, eng):
+    """Config 1: one encoder layer alone, L2 flushed before every timed step."""
+    import numpy as np
+    from laya_rust_b200 import workloads
+    torch = d.torch
+    req = workload("layer", d.rank)
+    plan = eng.plan(req)
+    real = plan.stats()[0]
+    x = np.random.default_rng(1 + d.rank).standard_normal((real, 1024)).astype(np.float16).astype(np.float32)
+    stream = ext_stream(d, eng)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")   # 256 MiB > 126 MB L2
+    clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
+    per_kind = {}
+    for kind, layer in LAYERS:
+        plan.set_hidden(x)
+        for _ in range(args.warmup):
+            plan.run_layer(layer)
+        torch.cuda.synchronize()
+        d.barrier()
+        evs = []
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                flush.zero_()
+                a = torch.cuda.Event(enable_timing=True)
+                b = torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                plan.run_layer(layer)
+                b.record(stream)
+                evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        per_kind[kind] = {"layer": layer, "ms": d.allmax(ms)}
+    clk = clocks.stop() if clocks else None
+    y = plan.hidden()
+    assert np.all(np.isfinite(y))
+
+    pk, pk_src = peaks()
+    peak = pk["bf16_tflops"]
+    for kind, layer in LAYERS:
+        g, a = layer_flops(req, kind == "global")
+        per_kind[kind]["tflops"] = (g + a) / (per_kind[kind]["ms"] / 1e3) / 1e12
+        per_kind[kind]["gemm_flops"], per_kind[kind]["attention_flops"] = g, a
+    mean_ms = sum(v["ms"] for v in per_kind.values()) / len(per_kind)
+    total_real = d.allsum(real)
+    value = total_real / (mean_ms / 1e3)
+    flops = sum(v["gemm_flops"] + v["attention_flops"] for v in per_kind.values())
+    achieved = flops / (sum(v["ms"] for v in per_kind.values()) / 1e3) / 1e12
+
+    # e2e: host residual stream in, one layer, host residual stream out
+    d.barrier()
+    e_ms = []
+    for i in range(args.steps):
+        kind, layer = LAYERS[i % len(LAYERS)]
+        e0 = time.perf_counter()
+        plan.set_hidden(x)
+        plan.run_layer(layer)
+        plan.hidden()
+        e_ms.append((time.perf_counter() - e0) * 1e3)
+    e_sec = d.allmax(sum(e_ms) / 1e3)
+    e2e = {"value": total_real * args.steps / e_sec, "unit": UNIT, "h2d_bytes_per_step": real * 4096,
+           "d2h_bytes_per_step": real * 4096, "ms_per_step": e_sec * 1e3 / args.steps,
+           "path": "laya_plan_set_hidden (H2D f32 stream) + laya_plan_run_layer + laya_plan_hidden (D2H)"}
+
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        sample = sub_request(req, 2 * args.cpu_sample)
+        sec = cpu_layer_run(sample, 1, 0)
+        cpu = cpu_baseline_line(workloads.real_tokens(sample) / sec, UNIT,
+                                f"first {sample.n} sequences ({workloads.real_tokens(sample)} real / "
+                                f"{sample.n * sample.l} padded tokens), layers 3 and 1 once each")
+    if d.rank == 0:
+        cfg = config_of(args, req, d.world)
+        cfg["l2"] = "flushed (256 MiB memset) before every timed step"
+        cfg["layers"] = {k: v for k, v in LAYERS}
+        line = base_line(args, METRIC + " (one encoder layer)", value, UNIT, d.world, mean_ms, cfg,
+                         padded_tokens_per_s=d.allsum(req.n * req.l) / (mean_ms / 1e3), layers=per_kind,
+                         roofline={"bound": "tensor", "kernel": "one encoder layer (4 tcgen05 GEMMs, attention, 2 norms)",
+                                   "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                                   "peak_source": f"{pk_src} bf16_tflops (burst: a layer is timed alone)",
+                                   "traffic": None},
+                         e2e=e2e, gpu_launches=layer_launches(req) * args.steps * len(LAYERS), clocks=clk,
+                         cpu_baseline=cpu)
+        print(json.dumps(line), flush=True)
+    plan.close()
+
+
+def run_request(args, d, eng):
+    """Config 0: latency of one System One request through the request path."""
+    from laya_rust_b200 import batching, workloads
+    torch = d.torch
+    items = workloads.single_request(0)
+    groups = batching.group_by_budget(items, 16384)
+    reqs = [batching.build_batch(items, g) for g in groups]
+    toks = sum(len(i.seq) for i in items)
+
+    # device time of the request's forwards (plans replayed as graphs)
+    plans = [eng.plan(r) for r in reqs]
+    for p in plans:
+        p.capture()
+    stream = ext_stream(d, eng)
+    for _ in range(args.warmup):
+        for p in plans:
+            p.run()
+    torch.cuda.synchronize()
+    d.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(args.steps):
+        for p in plans:
+            p.run()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    dev_ms = d.allmax(t0.elapsed_time(t1) / args.steps)
+    launches = sum(p.stats()[1] for p in plans)
+    upload = sum(p.stats()[2] for p in plans)
+    for p in plans:
+        p.close()
+
+    clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
+    for _ in range(args.warmup):
+        batching.run_all(eng, items)
+    d.barrier()
+    times = []
+    for _ in range(args.steps):
+        e0 = time.perf_counter()
+        batching.run_all(eng, items)
+        times.append((time.perf_counter() - e0) * 1e3)
+    clk = clocks.stop() if clocks else None
+    lat = latency_summary(times)
+    p50 = d.allmax(lat["p50"])
+
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        ct = cpu_request_run(items, 1, 0)
+        cpu = cpu_baseline_line(ct[0], "ms", f"the same request ({len(items)} questions, {toks} tokens), one run")
+    if d.rank == 0:
+        cfg = {"workload": "request", "model": MODEL, "questions": len(items), "forwards": len(reqs),
+               "real_tokens": toks, "seq_lens": [len(i.seq) for i in items],
+               "markers": [len(i.markers) for i in items], "parallelism": f"replicas{d.world}",
+               "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
+        e2e = {"value": p50, "unit": "ms", "h2d_bytes_per_step": upload,
+               "d2h_bytes_per_step": sum(4 * (r.n * r.k + 2 * r.n) for r in reqs),
+               "path": "batching.run_all -> laya_forward per forward group, scoring on host"}
+        line = base_line(args, LAT_METRIC, p50, "ms", d.world, lat["mean"], cfg, hib=False,
+                         latency_ms=lat, device_ms_per_request=dev_ms,
+                         tokens_per_s=toks / (lat["mean"] / 1e3), e2e=e2e,
+                         gpu_launches=launches * args.steps, clocks=clk, cpu_baseline=cpu)
+        print(json.dumps(line), flush=True)
+
+
+def run_stream(args, d, eng):
+    """Config 4: the request stream, dealt round-robin, packed per GPU."""
+    import numpy as np
+    from laya_rust_b200 import batching, workloads
+    torch = d.torch
+    reqs = workloads.request_stream(args.requests, 4)
+    mine = list(range(d.rank, len(reqs), d.world))
+    fws = workloads.pack_stream([reqs[i] for i in mine])
+    batches = [batching.build_batch(items, list(range(len(items)))) for items, _ in fws]
+    plans = [eng.plan(b) for b in batches]
+    real = sum(p.stats()[0] for p in plans)
+    launches = sum(p.stats()[1] for p in plans)
+    upload = sum(p.stats()[2] for p in plans)
+    padded = sum(b.n * b.l for b in batches)
+    stream = ext_stream(d, eng)
+
+    # warm-up: the forwards with the most rows, markers, sequences and the
+    # longest rows (they size the activation arena and the RoPE tables), then
+    # the first W
+    idx = range(len(plans))
+    big = {max(idx, key=lambda i: plans[i].stats()[0]), max(idx, key=lambda i: batches[i].n * batches[i].k),
+           max(idx, key=lambda i: batches[i].n), max(idx, key=lambda i: batches[i].l)}
+    for i in sorted(big) + list(range(min(args.warmup, len(plans)))):
+        plans[i].run()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
+    d.barrier()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for p in plans:
+        p.run()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    ms_max = d.allmax(ms)
+    for p in plans:
+        p.close()
+
+    # e2e: every forward through laya_forward, scored on the host; a request's
+    # service latency runs from the start of the forward holding its first
+    # question to the end of the one holding its last; its completion time is
+    # measured from the start of the pass (all requests queued at t = 0).
+    cal = batching.Calibration()
+    d.barrier()
+    start = time.perf_counter()
+    t_beg, t_end = [], []
+    for (items, ids), b in zip(fws, batches):
+        t_beg.append(time.perf_counter() - start)
+        out = eng.forward(b)
+        for row, it in enumerate(items):
+            batching.score_row(out.logits, out.act, row, b.k, len(it.markers), it.qtype, cal)
+        t_end.append(time.perf_counter() - start)
+    e_sec = d.allmax(time.perf_counter() - start)
+    clk = clocks.stop() if clocks else None
+    first, last = {}, {}
+    for f, (_, ids) in enumerate(fws):
+        for r, _ in ids:
+            first.setdefault(r, f)
+            last[r] = f
+    service = [(t_end[last[r]] - t_beg[first[r]]) * 1e3 for r in first]
+    completion = [t_end[last[r]] * 1e3 for r in first]
+    all_service = [v for part in d.gather(service) for v in part]
+    all_completion = [v for part in d.gather(completion) for v in part]
+    total_real = d.allsum(real)
+    forwards = d.allsum(len(fws))
+
+    cpu = None
+    if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
+        items = stream_sample()
+        ct = cpu_request_run(items, 1, 0)
+        toks = sum(len(i.seq) for i in items)
+        cpu = cpu_baseline_line(toks / (ct[0] / 1e3), UNIT,
+                                f"first 4 questions of request 0 ({toks} tokens) through run_all, one run")
+    if d.rank == 0:
+        cfg = {"workload": "stream", "model": MODEL, "requests": len(reqs),
+               "questions": sum(len(r) for r in reqs), "forwards": int(forwards),
+               "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
+               "parallelism": f"request-dp{d.world} (round-robin requests, no collective)",
+               "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
+        steps = len(fws)
+        e2e = {"value": total_real / e_sec, "unit": UNIT, "h2d_bytes_per_step": upload / steps,
+               "d2h_bytes_per_step": sum(4 * (b.n * b.k + 2 * b.n) for b in batches) / steps,
+               "makespan_s": e_sec, "service_latency_ms": latency_summary(all_service),
+               "completion_latency_ms": latency_summary(all_completion),
+               "path": "laya_forward per packed forward, scoring on host"}
+        line = base_line(args, METRIC + " (request stream)", total_real / (ms_max / 1e3), UNIT, d.world,
+                         ms_max / steps, cfg, padded_tokens_per_s=d.allsum(padded) / (ms_max / 1e3),
+                         device_makespan_s=ms_max / 1e3, e2e=e2e, gpu_launches=launches, clocks=clk,
+                         cpu_baseline=cpu)
+        line["steps"] = steps
+        line["warmup"] = min(args.warmup, len(plans)) + len(big)
+        print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    d = Dist()
+    eng = open_engine(d)
+    try:
+        if args.config in ("forward-16k", "long-state"):
+            run_forward(args, d, eng)
+        elif args.config == "layer":
+            run_layer(args, d, eng)
+        elif args.config == "request":
+            run_request(args, d, eng)
+        else:
+            run_stream(args, d, eng)
+    finally:
+        eng.close()
+        d.close()
 
 
 def main():

@@ -736,6 +736,51 @@ struct Engine {
     return nl;
   }
 
+  // One encoder layer (1..27) on the arena's residual stream, the body of the
+  // layer loop of graph.rs:103-123: LN, QKV + RoPE, attention, Wo + residual,
+  // LN, Wi + GeGLU, Wo_mlp + residual.
+  int64_t enqueue_layer(DevicePlan& dp, int layer) {
+    ensure_maps(dp);
+    const PlanMaps& M = dp.maps;
+    const HostPlan& p = dp.host;
+    const PlanLayout& L = dp.lay;
+    const int R = p.R;
+    int64_t nl = 0;
+    const bool global = layer % GLOBAL_EVERY == 0;
+    AttnArgs aa{qkv.as<__half>(), ctx.as<__half>(), dp.at<int>(L.seq_start), dp.at<int>(L.seq_len),
+                dp.at<int2>(L.blocks), global ? -1 : WINDOW};
+    ck(launch_ln(x.as<float>(), nullptr, W(attn_norm(layer)).buf.as<float>(), nullptr, EPS, t16.as<__half>(), R,
+                 stream),
+       "ln");
+    ++nl;
+    GemmArgs g{};
+    g.out = qkv.p;
+    g.ldo = 3 * H;
+    g.pos = dp.at<int>(L.pos);
+    g.cosb = global ? cos_full.as<float>() : cos_slide.as<float>();
+    g.sinb = global ? sin_full.as<float>() : sin_slide.as<float>();
+    g.scale = SCALE;
+    gemm(kEpiQkvRope, M.a_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), M.o_qkv, R, 3 * H, H, g, nl,
+         kProfQkv);
+    attention(M, aa, p, nl);
+    GemmArgs r{};
+    r.out = x.p;
+    r.ldo = H;
+    gemm(kEpiResid, M.a_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), M.o_x, R, H, H, r, nl, kProfWo);
+    ck(launch_ln(x.as<float>(), nullptr, W(fmt("encoder.layers.%d.mlp_norm.weight", layer)).buf.as<float>(), nullptr,
+                 EPS, t16.as<__half>(), R, stream),
+       "ln");
+    ++nl;
+    GemmArgs gg{};
+    gg.out = gate.p;
+    gg.ldo = INTER;
+    gg.n_valid = INTER;
+    gemm(kEpiGeglu, M.a_t16, W(fmt("encoder.layers.%d.mlp.Wi.weight", layer)), M.o_gate, R, 2 * INTER_PAD, H, gg, nl,
+         kProfWi);
+    gemm(kEpiResid, M.a_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), M.o_x, R, H, INTER, r, nl, kProfWo2);
+    return nl;
+  }
+
   // Diagnostic: copies the residual stream back and scatters it to padded rows.
   void emit_rows(const DevicePlan& dp, const char* stage, laya_tap_fn tap, void* user) {
     const HostPlan& p = dp.host;
@@ -1150,6 +1195,41 @@ int laya_plan_profile(laya_engine* e, laya_plan* p, int steps, double* ms, int64
 void laya_plan_destroy(laya_plan* p) { delete p; }
 
 void* laya_stream(laya_engine* e) { return e ? (void*)e->e->stream : nullptr; }
+
+int laya_plan_set_hidden(laya_engine* e, laya_plan* p, const float* x) {
+  return guard([&] {
+    if (!e || !p || !x) throw Error(LAYA_E_INVALID, "null argument");
+    Engine& g = *e->e;
+    g.set_device();
+    g.ensure_arena(p->dp.host);
+    laya::ck(cudaMemcpyAsync(g.x.p, x, (size_t)p->dp.host.R * laya::H * 4, cudaMemcpyHostToDevice, g.stream),
+             "hidden upload");
+    laya::ck(cudaStreamSynchronize(g.stream), "sync");
+  });
+}
+
+int laya_plan_hidden(laya_engine* e, laya_plan* p, float* x) {
+  return guard([&] {
+    if (!e || !p || !x) throw Error(LAYA_E_INVALID, "null argument");
+    Engine& g = *e->e;
+    g.set_device();
+    if (!g.x.p || g.cap_rows < p->dp.host.R) throw Error(LAYA_E_STATE, "no residual stream for this plan");
+    laya::ck(cudaStreamSynchronize(g.stream), "sync");
+    g.check_device_error();
+    laya::ck(cudaMemcpy(x, g.x.p, (size_t)p->dp.host.R * laya::H * 4, cudaMemcpyDeviceToHost), "hidden download");
+  });
+}
+
+int laya_plan_run_layer(laya_engine* e, laya_plan* p, int layer) {
+  return guard([&] {
+    if (!e || !p) throw Error(LAYA_E_INVALID, "null argument");
+    if (layer < 1 || layer >= laya::NLAYER) throw Error(LAYA_E_INVALID, "layer out of range (1..27)");
+    Engine& g = *e->e;
+    g.set_device();
+    g.ensure_arena(p->dp.host);
+    g.enqueue_layer(p->dp, layer);
+  });
+}
 
 int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float* out, int m, int n, int k,
                        int tile_n) {

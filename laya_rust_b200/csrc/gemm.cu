@@ -19,7 +19,8 @@
 //               BN=256); both CTAs' loads complete on the leader's barrier
 //   warp 1      TMEM allocation (both CTAs); MMA issue (leader only);
 //               accumulators double-buffered in TMEM (2 x BN columns)
-//   warps 2-5   epilogue: tcgen05.ld of 32 TMEM lanes, fused math, a
+//   warps 2-9   epilogue, two warps per TMEM lane quarter (one per column
+//               half of the tile): tcgen05.ld of 32 lanes, fused math, a
 //               128-byte-swizzled shared staging tile, then a TMA store
 //               (or TMA reduce-add for the f32 residual) of 32 rows at a time
 // No TMA load in this kernel uses multicast; every CTA loads its own operand

@@ -107,7 +107,7 @@ cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb,
 
 // ---- tail: scorer sum, post, act head --------------------------------------------
 struct TailArgs {
-  const float* partial;   // [4][ldp] scorer partial sums
+  const float* partial;   // [kScorerPartials][ldp] scorer partial sums
   int ldp;
   float score_bias;
   const int8_t* mmask;    // [n*k]

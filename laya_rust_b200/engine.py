@@ -17,6 +17,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
+from . import arch
+
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "_lib", "liblaya_b200.so")
 
@@ -69,6 +71,9 @@ def lib():
         L.laya_plan_profile.argtypes = [vp, vp, ctypes.c_int, ctypes.POINTER(ctypes.c_double), _i64p]
         L.laya_plan_destroy.argtypes = [vp]
         L.laya_plan_destroy.restype = None
+        L.laya_plan_set_hidden.argtypes = [vp, vp, _f32p]
+        L.laya_plan_run_layer.argtypes = [vp, vp, ctypes.c_int]
+        L.laya_plan_hidden.argtypes = [vp, vp, _f32p]
         L.laya_stream.argtypes = [vp]
         L.laya_stream.restype = vp
         L.laya_decision_tail_static.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp]
@@ -152,6 +157,21 @@ class Plan:
         _check(lib().laya_plan_outputs(self._e._h, self._h, logits.ctypes.data_as(_f32p),
                                        act.ctypes.data_as(_f32p)))
         return Out(r.n, r.k, logits, act)
+
+    def set_hidden(self, x: np.ndarray) -> None:
+        """Residual stream of the real tokens, [real_tokens, 1024] f32."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        _check(lib().laya_plan_set_hidden(self._e._h, self._h, x.ctypes.data_as(_f32p)))
+
+    def run_layer(self, layer: int) -> None:
+        """Enqueues encoder layer `layer` (1..27) alone on the current residual stream."""
+        _check(lib().laya_plan_run_layer(self._e._h, self._h, layer))
+
+    def hidden(self) -> np.ndarray:
+        """Synchronizes and returns the residual stream, [real_tokens, 1024] f32."""
+        x = np.empty((self.stats()[0], arch.H), np.float32)
+        _check(lib().laya_plan_hidden(self._e._h, self._h, x.ctypes.data_as(_f32p)))
+        return x
 
     PROF_KINDS = ["gemm_qkv", "gemm_attn_out", "gemm_ffn_in_geglu", "gemm_ffn_out", "gemm_head_scorer",
                   "attention", "row_norms", "tail"]

@@ -61,6 +61,107 @@ def long_state(seed: int = 3) -> Req:
     return padded_batch(rng, [512] * 8, 512, markers_lo=3, markers_hi=3, qtypes=[0] * 8)
 
 
+def layer_batch(seed: int = 1) -> Req:
+    """Config 1 (one encoder layer in isolation): 32 sequences padded to 256,
+    real lengths uniform in [16, 256]."""
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(16, 257, 32)
+    return padded_batch(rng, lens, 256)
+
+
+# ---- System One requests at the token level -----------------------------------------
+# The real tokenizer is not available, so a word is one token drawn from the
+# non-special vocabulary; the sequence layout is the reference's
+# (systemone.rs:156-198): [CLS] head [SEP] ([MASK] option)* [SEP] state [SEP],
+# options cut to 48 tokens, the whole sequence to 512.
+
+NOUL_FALSE_TOKENS = 9   # " false: no, the statement does not hold"
+NOUL_TRUE_TOKENS = 7    # " true: yes, the statement holds"
+
+
+def _words(rng, n):
+    return list(rng.integers(0, NON_SPECIAL, int(n)))
+
+
+def question_item(rng, state, qtype, instr_words, options):
+    """One question -> Item(seq, markers, qtype) (systemone.rs:156-198)."""
+    from .batching import Item
+    head = _words(rng, 3 + instr_words)              # "<type> question: <instructions>"
+    ids = [arch.CLS_ID] + head + [arch.SEP_ID]
+    markers = []
+    for opt in options:
+        markers.append(len(ids))
+        ids += [arch.MASK_ID] + opt[:48]
+    ids.append(arch.SEP_ID)
+    room = max(0, arch.MAX_LEN - (len(ids) + 1))
+    ids += state[:room]
+    ids.append(arch.SEP_ID)
+    ids = ids[:arch.MAX_LEN]
+    markers = [m for m in markers if m < arch.MAX_LEN]
+    return Item(ids, markers, qtype)
+
+
+def system_one_request(rng, state_words, questions):
+    """questions: list of ("choice", criteria_word_counts, instr_words) or
+    ("noul", instr_words)."""
+    state = _words(rng, state_words)
+    items = []
+    for q in questions:
+        if q[0] == "choice":
+            opts = [_words(rng, c) for c in q[1]]
+            items.append(question_item(rng, state, 0, q[2], opts))
+        else:
+            opts = [_words(rng, NOUL_FALSE_TOKENS), _words(rng, NOUL_TRUE_TOKENS)]
+            items.append(question_item(rng, state, 2, q[1], opts))
+    return items
+
+
+def single_request(seed: int = 0):
+    """Config 0: a 48-word state, one choice question with 2 criteria of 6
+    words, one noul question with 12-word instructions."""
+    rng = np.random.default_rng(seed)
+    return system_one_request(rng, 48, [("choice", [6, 6], 8), ("noul", 12)])
+
+
+def request_stream(n_requests: int = 4096, seed: int = 4):
+    """Config 4: per request, state length lognormal (median 96 tokens,
+    sigma 0.8, capped at 1024), 1..16 questions, choice (2..6 criteria of
+    3..8 tokens) and noul 1:1, instructions 8..16 tokens."""
+    rng = np.random.default_rng(seed)
+    reqs = []
+    for _ in range(n_requests):
+        state = int(min(1024, round(float(rng.lognormal(np.log(96.0), 0.8)))))
+        qs = []
+        for _ in range(int(rng.integers(1, 17))):
+            instr = int(rng.integers(8, 17))
+            if rng.random() < 0.5:
+                qs.append(("choice", list(rng.integers(3, 9, int(rng.integers(2, 7)))), instr))
+            else:
+                qs.append(("noul", instr))
+        reqs.append(system_one_request(rng, state, qs))
+    return reqs
+
+
+def pack_stream(requests, max_tokens: int = 16384):
+    """Cross-request packing in dispatch order: items join the current forward
+    while max_len * count stays within the budget (the budget rule of
+    main.rs:448-468, applied across requests).  Returns [(items, [(request,
+    item index)])] per forward."""
+    forwards, cur, cur_ids, cur_max = [], [], [], 0
+    for ri, items in enumerate(requests):
+        for ii, it in enumerate(items):
+            ln = len(it.seq)
+            if cur and max(cur_max, ln) * (len(cur) + 1) > max_tokens:
+                forwards.append((cur, cur_ids))
+                cur, cur_ids, cur_max = [], [], 0
+            cur.append(it)
+            cur_ids.append((ri, ii))
+            cur_max = max(cur_max, ln)
+    if cur:
+        forwards.append((cur, cur_ids))
+    return forwards
+
+
 def real_tokens(req: Req) -> int:
     return int((req.att != 0).sum())
 

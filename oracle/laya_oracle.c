@@ -837,6 +837,43 @@ static float *fa(size_t n) {
     return p;
 }
 
+/* One encoder layer 1..NLAYER-1 in place on the padded residual stream
+ * x [n*l, H]: the body of the layer loop of graph.rs:104-123 (layers > 0 add
+ * the attention output to x).  Returns -1 on bad arguments. */
+int lo_encoder_layer(const lo_model *m, size_t n, size_t l, const int64_t *att, int layer,
+                     float *x) {
+    if (!(n > 0 && l > 0) || layer < 1 || layer >= NLAYER) return -1;
+    size_t rows = n * l, half = HD / 2;
+    int global = layer % GLOBAL_EVERY == 0;
+    float *cs = fa(l * half), *sn = fa(l * half), *mask = fa(n * l * l);
+    lo_rope_tables(W(m, global ? "rope.freq_full" : "rope.freq_sliding")->data, l, cs, sn);
+    lo_window_mask(att, n, l, global ? -1 : WINDOW, mask);
+    float *t = fa(rows * H), *qkv = fa(rows * 3 * H), *q = fa(rows * H), *kk = fa(rows * H),
+          *v = fa(rows * H), *ctx = fa(rows * H), *p = fa(rows * H), *mlp = fa(rows * 2 * INTER),
+          *gate = fa(rows * INTER);
+    char nm[96];
+    snprintf(nm, sizeof nm, "encoder.layers.%d.attn_norm.weight", layer);
+    lo_layernorm(x, rows, H, W(m, nm)->data, NULL, EPS, t);
+    snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wqkv.weight", layer);
+    lo_matmul(t, rows, H, W(m, nm)->data, 3 * H, qkv);
+    lo_split_qkv_rope(qkv, rows, cs, sn, SCALE, NH, HD, l, q, kk, v);
+    lo_attention(q, kk, v, mask, n, NH, l, HD, ctx);
+    snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wo.weight", layer);
+    lo_matmul(ctx, rows, H, W(m, nm)->data, H, p);
+    lo_add(x, p, rows * H, x);
+    snprintf(nm, sizeof nm, "encoder.layers.%d.mlp_norm.weight", layer);
+    lo_layernorm(x, rows, H, W(m, nm)->data, NULL, EPS, t);
+    snprintf(nm, sizeof nm, "encoder.layers.%d.mlp.Wi.weight", layer);
+    lo_matmul(t, rows, H, W(m, nm)->data, 2 * INTER, mlp);
+    lo_gelu_mul(mlp, rows, INTER, gate);
+    snprintf(nm, sizeof nm, "encoder.layers.%d.mlp.Wo.weight", layer);
+    lo_matmul(gate, rows, INTER, W(m, nm)->data, H, p);
+    lo_add(x, p, rows * H, x);
+    free(cs); free(sn); free(mask); free(t); free(qkv); free(q); free(kk); free(v); free(ctx);
+    free(p); free(mlp); free(gate);
+    return 0;
+}
+
 /* graph.rs:86-186.  layer_limit < 0 runs all NLAYER encoder layers. */
 int lo_forward_ex(const lo_model *m, size_t n, size_t l, size_t k, const int64_t *ids,
                   const int64_t *att, const int64_t *mpos, const int64_t *mmask,

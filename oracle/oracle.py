@@ -43,6 +43,8 @@ def lib():
         L.lo_forward_ex.restype = ctypes.c_int
         L.lo_forward_ex.argtypes = [ctypes.c_void_p, _sz, _sz, _sz, _i64p, _i64p, _i64p, _i64p,
                                     _i64p, _f32p, _f32p, TAP_FN, ctypes.c_void_p]
+        L.lo_encoder_layer.restype = ctypes.c_int
+        L.lo_encoder_layer.argtypes = [ctypes.c_void_p, _sz, _sz, _i64p, ctypes.c_int, _f32p]
         L.lo_f2h.restype = ctypes.c_uint16
         L.lo_f2h.argtypes = [ctypes.c_float]
         L.lo_h2f.restype = ctypes.c_float
@@ -266,3 +268,12 @@ class OracleModel:
         if rc != 0:
             raise RuntimeError("oracle forward rejected the request")
         return logits, act
+
+    def encoder_layer(self, n, l, att, layer, x):
+        """One encoder layer (1..27, graph.rs:104-123) on the padded residual
+        stream x [n*l, 1024]; returns the new stream."""
+        att = _i(att)
+        y = np.ascontiguousarray(x, dtype=np.float32).reshape(n * l, 1024).copy()
+        if lib().lo_encoder_layer(self._h, n, l, _p(att, _i64p), layer, _p(y)) != 0:
+            raise RuntimeError("oracle encoder_layer rejected the arguments")
+        return y
