@@ -11,15 +11,15 @@ Workloads (--config), all seeded synthetic data on a random-init f16 model:
   long-state   config 3: 8 sequences x 512 tokens.  A step is one forward.
   layer        config 1: one encoder layer alone on 32 sequences padded to
                256 (real lengths U[16,256]), f16 N(0,1) activations; global
-               layer 3 and local layer 1 timed separately, L2 flushed before
+               layer 0 and local layer 1 timed separately, L2 flushed before
                every step (the layer's weights and activations fit in L2).
   request      config 0: one System One request (48-word state, a choice
                question with 2 criteria, a noul question) through the request
                path (group_by_budget, build_batch, forward, scoring); the
                metric is its latency (ms, p50 over the steps).
-  stream       config 4: 4096 seeded requests dealt round-robin to the GPUs;
-               each GPU packs its share into <=16384-token forwards.  Steps are
-               the forwards of one pass over the stream.
+  stream       config 4: 4096 seeded requests assigned to the GPUs greedily by
+               token cost; each GPU packs its share into <=16384-token
+               forwards.  Steps are the forwards of one pass over the stream.
 
   value     device-resident: requests uploaded once (plans), forwards
             enqueued back to back (CUDA graph replay where one plan repeats);
@@ -60,13 +60,13 @@ LAT_METRIC = "request latency p50"
 CONFIGS = ["forward-16k", "long-state", "layer", "request", "stream"]
 DATA = "synthetic (seeded ids, random-init weights)"
 MODEL = "laya (ModernBERT-large 28L + 2L head), random-init f16 GGUF seed 0"
-LAYERS = (("global", 3), ("local", 1))
+LAYERS = (("global", 0), ("local", 1))
 
 
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="forward-16k", choices=CONFIGS)
@@ -200,7 +200,9 @@ def stream_sample():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms; the
+    constructor returns once the first sample is written, so sampling is live
+    when the timed region starts."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -211,9 +213,13 @@ class ClockSampler:
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={','.join(map(str, gpus))}",
                                        f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
         except OSError:
             self.p = None
+            return
+        t_end = time.time() + 5.0
+        while time.time() < t_end and self.p.poll() is None and os.path.getsize(self.f.name) == 0:
+            time.sleep(0.02)
 
     def stop(self):
         if self.p is None:
@@ -270,7 +276,7 @@ def run_reference(args):
         real = workloads.real_tokens(sample)
         if args.config == "layer":
             sec = cpu_layer_run(sample, args.steps, args.warmup)
-            what = "one encoder layer (global layer 3 and local layer 1 alternately)"
+            what = "one encoder layer (global layer 0 and local layer 1 alternately)"
         else:
             sec = cpu_run(sample, args.steps, args.warmup)
             what = "one forward"
@@ -540,7 +546,7 @@ def run_layer(args, d, eng):
         sec = cpu_layer_run(sample, 1, 0)
         cpu = cpu_baseline_line(workloads.real_tokens(sample) / sec, UNIT,
                                 f"first {sample.n} sequences ({workloads.real_tokens(sample)} real / "
-                                f"{sample.n * sample.l} padded tokens), layers 3 and 1 once each")
+                                f"{sample.n * sample.l} padded tokens), layers 0 and 1 once each")
     if d.rank == 0:
         cfg = config_of(args, req, d.world)
         cfg["l2"] = "flushed (256 MiB memset) before every timed step"
@@ -623,17 +629,16 @@ def run_request(args, d, eng):
 
 
 def run_stream(args, d, eng):
-    """Config 4: the request stream, dealt round-robin, packed per GPU."""
+    """Config 4: the request stream, assigned greedily by cost, packed per GPU."""
     import numpy as np
     from laya_rust_b200 import batching, workloads
     torch = d.torch
     reqs = workloads.request_stream(args.requests, 4)
-    mine = list(range(d.rank, len(reqs), d.world))
+    mine = workloads.assign_requests(reqs, d.world)[d.rank]
     fws = workloads.pack_stream([reqs[i] for i in mine])
     batches = [batching.build_batch(items, list(range(len(items)))) for items, _ in fws]
     plans = [eng.plan(b) for b in batches]
     real = sum(p.stats()[0] for p in plans)
-    launches = sum(p.stats()[1] for p in plans)
     upload = sum(p.stats()[2] for p in plans)
     padded = sum(b.n * b.l for b in batches)
     stream = ext_stream(d, eng)
@@ -658,6 +663,7 @@ def run_stream(args, d, eng):
     torch.cuda.synchronize()
     ms = t0.elapsed_time(t1)
     ms_max = d.allmax(ms)
+    launches = sum(p.stats()[1] for p in plans)
     for p in plans:
         p.close()
 
@@ -700,7 +706,7 @@ def run_stream(args, d, eng):
         cfg = {"workload": "stream", "model": MODEL, "requests": len(reqs),
                "questions": sum(len(r) for r in reqs), "forwards": int(forwards),
                "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
-               "parallelism": f"request-dp{d.world} (round-robin requests, no collective)",
+               "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
                "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
         steps = len(fws)
         e2e = {"value": total_real / e_sec, "unit": UNIT, "h2d_bytes_per_step": upload / steps,

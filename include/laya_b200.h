@@ -116,12 +116,13 @@ void laya_plan_destroy(laya_plan *p);
 /* The cudaStream_t the engine launches on. */
 void *laya_stream(laya_engine *e);
 /* One encoder layer in isolation (a benchmark configuration, the body of the
- * layer loop of graph.rs:103-132): set the residual stream of the plan's real
+ * layer loop of graph.rs:103-123): set the residual stream of the plan's real
  * tokens (x: [real_tokens, 1024] f32, sequences back to back), enqueue layer
- * `layer` (attn_norm LN, QKV + RoPE, attention, Wo + residual, mlp_norm LN,
- * Wi + GeGLU, Wo_mlp + residual) on it, and read it back.  layer is 1..27:
- * layer 0 has no attn_norm of its own (its input norm is the embedding norm,
- * fused into the embedding kernel).  Global layers are the multiples of 3. */
+ * `layer` (0..27: input LN, QKV + RoPE, attention, Wo + residual, mlp_norm
+ * LN, Wi + GeGLU, Wo_mlp + residual) on it, and read it back.  Layer 0's input
+ * LN is the embedding norm and its residual base is the normed input
+ * (graph.rs:112-113), so for layer 0 x is the embedding output.  Global layers
+ * are the multiples of 3. */
 int laya_plan_set_hidden(laya_engine *e, laya_plan *p, const float *x);
 int laya_plan_run_layer(laya_engine *e, laya_plan *p, int layer);
 int laya_plan_hidden(laya_engine *e, laya_plan *p, float *x);

@@ -140,6 +140,8 @@ __global__ void __launch_bounds__(THREADS, Layout<kSingle>::MIN_BLOCKS)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Lay::BAR_OFF);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 3);
 
+  grid_dep_wait();
+  grid_dep_trigger();
   const int tid = threadIdx.x, warp = tid >> 5;
   const int2 blk = a.blocks[blockIdx.x];
   const int b = blk.x, q0 = blk.y, h = blockIdx.y;
@@ -364,8 +366,8 @@ cudaError_t launch_one(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_blo
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  attn_tc_kernel<kSingle><<<dim3(num_blocks, 16), THREADS, smem, stream>>>(*tm_qkv, a, err);
-  return cudaGetLastError();
+  return launch_pdl(attn_tc_kernel<kSingle>, dim3(num_blocks, 16), dim3(THREADS), smem, stream, nullptr, 0,
+                    *tm_qkv, a, err);
 }
 
 }  // namespace

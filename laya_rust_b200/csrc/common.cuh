@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace laya {
 
 // Error codes written to the device error word (first writer wins).
@@ -214,6 +216,46 @@ __device__ __forceinline__ float erf_as(float x) {
 __device__ __forceinline__ float gelu_erf(float v) {
   // exact-erf GELU (cpu/mod.rs:76-78): 0.5 v (1 + erf(v / sqrt 2))
   return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+}
+
+// ---- programmatic dependent launch ---------------------------------------------------
+// Every kernel is launched with programmatic stream serialization allowed, so
+// it may start while the kernel before it in the stream is still running.
+// Each kernel therefore calls grid_dep_wait() before its first access to
+// memory that a previous kernel writes or reads (everything except weights,
+// tensor maps and its own shared memory) -- the wait returns once the previous
+// grid has completed and its writes are visible, which by induction orders it
+// after every earlier kernel too -- and grid_dep_trigger() right after, which
+// lets the next kernel be scheduled into SM slots as they free up and run its
+// own prologue.  Without a programmatic predecessor the wait returns at once.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Host: whether launches carry the programmatic-serialization attribute
+// (LAYA_PDL=0 turns it off for the whole process).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with the programmatic-serialization attribute (when
+// enabled) and optional extra attributes.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[4];
+  int n = 0;
+  for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 }  // namespace laya

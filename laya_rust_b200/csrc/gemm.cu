@@ -27,11 +27,21 @@
 // halves.  The MMA completion signal is delivered to both CTAs of the pair
 // with tcgen05.commit's cluster-multicast form.
 #include <cstdio>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
 
 namespace laya {
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LAYA_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 
 namespace {
 
@@ -392,6 +402,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   cluster_sync();  // barrier inits and TMEM allocation visible cluster-wide
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // the prologue above touches only shared memory, TMEM and the tensor maps
+  grid_dep_wait();
+  grid_dep_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -520,19 +533,13 @@ cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cud
   if (num_tiles == 0) return cudaSuccess;
   const int max_clusters = num_sms / 2;
   const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters, 1, 1);
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = Cfg<BN>::SMEM;
-  cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<EPI, BN>, *m.a, *m.b, *m.out, args);
+  return launch_pdl(gemm_tc_kernel<EPI, BN>, dim3(2 * clusters, 1, 1), dim3(THREADS, 1, 1), Cfg<BN>::SMEM, stream,
+                    attr, 1, *m.a, *m.b, *m.out, args);
 }
 
 }  // namespace

@@ -100,6 +100,8 @@ cudaError_t launch_embed_ln(const __half* emb, const int* tok, const float* w, f
 // t16[r] = LN(x[src(r)]) * w (+ b); src(r) = idx ? idx[r] : r
 cudaError_t launch_ln(const float* x, const int* idx, const float* w, const float* b, float eps,
                       __half* t16, int rows, cudaStream_t s);
+// x[r] = t16[r] = LN(x[r]) * w  (each warp reads its row before writing it)
+cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, int rows, cudaStream_t s);
 // x[r] = LN(x[r]) * wf + type[rowtype[r]];  t16[r] = LN(x[r]) * w1 + b1
 cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb,
                             const uint8_t* rowtype, const float* w1, const float* b1,

@@ -98,6 +98,8 @@ __device__ __forceinline__ void scale_shift(float (&v)[32], int lane, const floa
 
 __global__ void __launch_bounds__(256) embed_ln_kernel(const __half* emb, const int* tok, const float* w,
                                                        float eps, float* x, __half* t16, int rows) {
+  grid_dep_wait();
+  grid_dep_trigger();
   const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -110,7 +112,9 @@ __global__ void __launch_bounds__(256) embed_ln_kernel(const __half* emb, const 
 }
 
 __global__ void __launch_bounds__(256) ln_kernel(const float* x, const int* idx, const float* w, const float* b,
-                                                 float eps, __half* t16, int rows) {
+                                                 float eps, __half* t16, float* xo, int rows) {
+  grid_dep_wait();
+  grid_dep_trigger();
   const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -119,6 +123,7 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const int* idx,
   load_f32(x + static_cast<size_t>(src) * HID, lane, v);
   normalize(v, eps);
   scale_shift(v, lane, w, b);
+  if (xo) store_f32(xo + static_cast<size_t>(row) * HID, lane, v);
   store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
 }
 
@@ -126,6 +131,8 @@ __global__ void __launch_bounds__(256) final_ln_kernel(float* x, const float* wf
                                                        const uint8_t* rowtype, const float* w1,
                                                        const float* b1, float eps, __half* t16,
                                                        int rows) {
+  grid_dep_wait();
+  grid_dep_trigger();
   const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -150,23 +157,29 @@ inline int grid_rows(int rows) { return (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA
 cudaError_t launch_embed_ln(const __half* emb, const int* tok, const float* w, float eps, float* x,
                             __half* t16, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  embed_ln_kernel<<<grid_rows(rows), 256, 0, s>>>(emb, tok, w, eps, x, t16, rows);
-  return cudaGetLastError();
+  return launch_pdl(embed_ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, emb, tok, w, eps, x, t16,
+                    rows);
 }
 
 cudaError_t launch_ln(const float* x, const int* idx, const float* w, const float* b, float eps,
                       __half* t16, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  ln_kernel<<<grid_rows(rows), 256, 0, s>>>(x, idx, w, b, eps, t16, rows);
-  return cudaGetLastError();
+  return launch_pdl(ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, idx, w, b, eps, t16,
+                    static_cast<float*>(nullptr), rows);
+}
+
+cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, int rows, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  return launch_pdl(ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, static_cast<const float*>(x),
+                    static_cast<const int*>(nullptr), w, static_cast<const float*>(nullptr), eps, t16, x, rows);
 }
 
 cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb, const uint8_t* rowtype,
                             const float* w1, const float* b1, float eps, __half* t16, int rows,
                             cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  final_ln_kernel<<<grid_rows(rows), 256, 0, s>>>(x, wf, type_emb, rowtype, w1, b1, eps, t16, rows);
-  return cudaGetLastError();
+  return launch_pdl(final_ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, wf, type_emb, rowtype,
+                    w1, b1, eps, t16, rows);
 }
 
 }  // namespace laya

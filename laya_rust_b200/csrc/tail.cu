@@ -32,6 +32,8 @@ __global__ void __launch_bounds__(256) tail_kernel(const TailArgs a) {
   float* ain = sm;             // [1028]
   float* hid = sm + AIN;       // [256]
   float* lg = hid + AH;        // [k]
+  grid_dep_wait();
+  grid_dep_trigger();
   const int b = blockIdx.x;
   const int k = a.k;
   const int tid = threadIdx.x;
@@ -103,8 +105,7 @@ cudaError_t launch_tail(const TailArgs& a, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
   const size_t smem = sizeof(float) * (AIN + AH + a.k);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
-  tail_kernel<<<a.n, 256, smem, s>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(tail_kernel, dim3(a.n), dim3(256), smem, s, nullptr, 0, a);
 }
 
 }  // namespace laya

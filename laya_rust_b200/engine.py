@@ -164,7 +164,8 @@ class Plan:
         _check(lib().laya_plan_set_hidden(self._e._h, self._h, x.ctypes.data_as(_f32p)))
 
     def run_layer(self, layer: int) -> None:
-        """Enqueues encoder layer `layer` (1..27) alone on the current residual stream."""
+        """Enqueues encoder layer `layer` (0..27) alone on the current residual
+        stream (for layer 0: the embedding output, before the embedding norm)."""
         _check(lib().laya_plan_run_layer(self._e._h, self._h, layer))
 
     def hidden(self) -> np.ndarray:

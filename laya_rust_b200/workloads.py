@@ -16,19 +16,20 @@ from .engine import Req
 NON_SPECIAL = 50280
 
 
-def _row(rng, r, n_markers):
-    """One sequence of length r with n_markers [MASK] markers after a mid [SEP]."""
+def _row(rng, r, n_markers, head=None):
+    """One sequence of length r with n_markers [MASK] markers after the [SEP]
+    closing a question head of `head` tokens (default r // 3)."""
     ids = rng.integers(0, NON_SPECIAL, r)
     ids[0] = arch.CLS_ID
     ids[r - 1] = arch.SEP_ID
-    head = max(2, min(r // 3, r - n_markers - 3))
+    head = max(2, min(r // 3 if head is None else head, r - n_markers - 3))
     ids[head] = arch.SEP_ID
     pos = np.sort(rng.choice(np.arange(head + 1, r - 1), size=n_markers, replace=False))
     ids[pos] = arch.MASK_ID
     return ids, pos
 
 
-def padded_batch(rng, lens, l, markers_lo=2, markers_hi=6, qtypes=None) -> Req:
+def padded_batch(rng, lens, l, markers_lo=2, markers_hi=6, qtypes=None, head=None) -> Req:
     n = len(lens)
     nms = [int(rng.integers(markers_lo, markers_hi + 1)) for _ in lens]
     k = max(nms)
@@ -37,7 +38,7 @@ def padded_batch(rng, lens, l, markers_lo=2, markers_hi=6, qtypes=None) -> Req:
     mpos = np.zeros((n, k), np.int64)
     mmask = np.zeros((n, k), np.int64)
     for b, (r, nm) in enumerate(zip(lens, nms)):
-        row, pos = _row(rng, r, nm)
+        row, pos = _row(rng, r, nm, head)
         ids[b, :r] = row
         att[b, :r] = 1
         mpos[b, :nm] = pos
@@ -55,10 +56,11 @@ def forward_16k(seed: int = 0) -> Req:
 
 
 def long_state(seed: int = 3) -> Req:
-    """Config 3: 8 sequences at the maximum position length (512): ~32 tokens
-    of question head with 3 criteria markers, state filling the rest."""
+    """Config 3: 8 sequences at the maximum position length (512), i.e. two
+    requests of 4 choice questions: a 32-token question head, 3 criteria
+    markers after it, the state filling the rest."""
     rng = np.random.default_rng(seed)
-    return padded_batch(rng, [512] * 8, 512, markers_lo=3, markers_hi=3, qtypes=[0] * 8)
+    return padded_batch(rng, [512] * 8, 512, markers_lo=3, markers_hi=3, qtypes=[0] * 8, head=32)
 
 
 def layer_batch(seed: int = 1) -> Req:
@@ -140,6 +142,19 @@ def request_stream(n_requests: int = 4096, seed: int = 4):
                 qs.append(("noul", instr))
         reqs.append(system_one_request(rng, state, qs))
     return reqs
+
+
+def assign_requests(requests, world: int):
+    """Greedy assignment of requests (in dispatch order) to `world` GPUs: each
+    request goes to the GPU with the least padded-token cost so far, its cost
+    being the sum of its sequence lengths.  Returns the request indices per GPU."""
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for ri, items in enumerate(requests):
+        g = min(range(world), key=lambda i: (load[i], i))
+        out[g].append(ri)
+        load[g] += sum(len(it.seq) for it in items)
+    return out
 
 
 def pack_stream(requests, max_tokens: int = 16384):

@@ -837,12 +837,13 @@ static float *fa(size_t n) {
     return p;
 }
 
-/* One encoder layer 1..NLAYER-1 in place on the padded residual stream
- * x [n*l, H]: the body of the layer loop of graph.rs:104-123 (layers > 0 add
- * the attention output to x).  Returns -1 on bad arguments. */
+/* One encoder layer 0..NLAYER-1 in place on the padded residual stream
+ * x [n*l, H]: the body of the layer loop of graph.rs:104-123 (layer 0 norms
+ * with the embedding norm and adds the attention output to the normed input,
+ * later layers add it to x).  Returns -1 on bad arguments. */
 int lo_encoder_layer(const lo_model *m, size_t n, size_t l, const int64_t *att, int layer,
                      float *x) {
-    if (!(n > 0 && l > 0) || layer < 1 || layer >= NLAYER) return -1;
+    if (!(n > 0 && l > 0) || layer < 0 || layer >= NLAYER) return -1;
     size_t rows = n * l, half = HD / 2;
     int global = layer % GLOBAL_EVERY == 0;
     float *cs = fa(l * half), *sn = fa(l * half), *mask = fa(n * l * l);
@@ -852,7 +853,8 @@ int lo_encoder_layer(const lo_model *m, size_t n, size_t l, const int64_t *att, 
           *v = fa(rows * H), *ctx = fa(rows * H), *p = fa(rows * H), *mlp = fa(rows * 2 * INTER),
           *gate = fa(rows * INTER);
     char nm[96];
-    snprintf(nm, sizeof nm, "encoder.layers.%d.attn_norm.weight", layer);
+    if (layer == 0) snprintf(nm, sizeof nm, "encoder.embeddings.norm.weight");
+    else snprintf(nm, sizeof nm, "encoder.layers.%d.attn_norm.weight", layer);
     lo_layernorm(x, rows, H, W(m, nm)->data, NULL, EPS, t);
     snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wqkv.weight", layer);
     lo_matmul(t, rows, H, W(m, nm)->data, 3 * H, qkv);
@@ -860,7 +862,7 @@ int lo_encoder_layer(const lo_model *m, size_t n, size_t l, const int64_t *att, 
     lo_attention(q, kk, v, mask, n, NH, l, HD, ctx);
     snprintf(nm, sizeof nm, "encoder.layers.%d.attn.Wo.weight", layer);
     lo_matmul(ctx, rows, H, W(m, nm)->data, H, p);
-    lo_add(x, p, rows * H, x);
+    lo_add(layer == 0 ? t : x, p, rows * H, x);
     snprintf(nm, sizeof nm, "encoder.layers.%d.mlp_norm.weight", layer);
     lo_layernorm(x, rows, H, W(m, nm)->data, NULL, EPS, t);
     snprintf(nm, sizeof nm, "encoder.layers.%d.mlp.Wi.weight", layer);

@@ -270,7 +270,7 @@ class OracleModel:
         return logits, act
 
     def encoder_layer(self, n, l, att, layer, x):
-        """One encoder layer (1..27, graph.rs:104-123) on the padded residual
+        """One encoder layer (0..27, graph.rs:104-123) on the padded residual
         stream x [n*l, 1024]; returns the new stream."""
         att = _i(att)
         y = np.ascontiguousarray(x, dtype=np.float32).reshape(n * l, 1024).copy()

@@ -66,6 +66,9 @@ def synthetic_req(seed, lens, k, l=None):
     return Req(n, l, k, ids, att, mpos, mmask, qtype)
 
 
+SPLIT_LENS = [300, 40, 400, 128, 129, 77, 256, 200, 30, 390, 64, 100]
+
+
 def fixture_reqs():
     out = []
     for fx in FIXTURES:
@@ -80,6 +83,9 @@ CASES = fixture_reqs() + [
     ("window-3x200", synthetic_req(11, [200, 150, 70], 4)),
     ("maxlen-2x512", synthetic_req(12, [512, 300], 3)),
     ("ragged-8", synthetic_req(13, [24, 128, 77, 31, 128, 64, 65, 100], 5, l=128)),
+    # >= 2048 real tokens: with LAYA_ROW_GROUPS=2 the batch runs as two row
+    # groups on two streams
+    ("two-groups-12", synthetic_req(14, SPLIT_LENS, 4, l=400)),
 ]
 
 
@@ -123,17 +129,19 @@ def test_residual_stream_taps_track_the_oracle(engine, oracle):
     assert np.array_equal(taps_g["logits"], engine.forward(req).logits)
 
 
-@pytest.mark.parametrize("layer", [1, 3, 27])
-def test_single_layer_matches_the_oracle_layer(layer, engine, oracle):
+@pytest.mark.parametrize("layer,lens", [(0, [200, 150, 70]), (1, [200, 150, 70]), (3, [200, 150, 70]),
+                                        (27, [200, 150, 70]), (0, SPLIT_LENS), (1, SPLIT_LENS)])
+def test_single_layer_matches_the_oracle_layer(layer, lens, engine, oracle):
     """One encoder layer in isolation (the single-layer benchmark
     configuration): the oracle's residual stream before layer i goes in, the
     engine's after layer i must match the oracle's enc.{i} tap.  Rows longer
-    than 129 tokens, so the local layers' window is active."""
-    req = synthetic_req(11, [200, 150, 70], 4)
+    than 129 tokens, so the local layers' window is active; the second
+    request has two row groups."""
+    req = synthetic_req(11, lens, 4, l=max(lens))
     taps = {}
     oracle.forward(req.n, req.l, req.k, req.ids, req.att, req.mpos, req.mmask, req.qtype, taps=taps)
     real = (req.att.reshape(req.n, req.l) != 0).ravel()
-    x_in = taps[f"enc.{layer - 1}"].reshape(-1, 1024)[real]
+    x_in = taps[f"enc.{layer - 1}" if layer else "embed"].reshape(-1, 1024)[real]
     want = taps[f"enc.{layer}"].reshape(-1, 1024)[real]
     p = engine.plan(req)
     p.set_hidden(x_in)
@@ -144,10 +152,11 @@ def test_single_layer_matches_the_oracle_layer(layer, engine, oracle):
     assert rel < 1e-2, rel
 
 
-def test_single_layer_rejects_layer_zero(engine):
+def test_single_layer_rejects_a_layer_out_of_range(engine):
     p = engine.plan(synthetic_req(12, [40], 2))
-    with pytest.raises(E.LayaError, match="layer"):
-        p.run_layer(0)
+    for layer in (-1, 28):
+        with pytest.raises(E.LayaError, match="layer"):
+            p.run_layer(layer)
     p.close()
 
 

@@ -1,7 +1,7 @@
 """The oracle's single-layer entry point (the CPU side of the one-layer
 benchmark configuration) is the body of its whole-forward layer loop: fed the
-enc.{i-1} tap it reproduces the enc.{i} tap bit for bit, on a ragged request
-with padding rows."""
+enc.{i-1} tap (the embed tap for layer 0) it reproduces the enc.{i} tap bit
+for bit, on a ragged request with padding rows."""
 import numpy as np
 import pytest
 
@@ -27,11 +27,12 @@ def test_encoder_layer_reproduces_the_forward_taps(oracle):
     mmask = np.ones((n, k), np.int64)
     taps = {}
     oracle.forward(n, l, k, ids, att, mpos, mmask, np.array([0, 2]), taps=taps)
-    for layer in (1, 3, 27):
-        y = oracle.encoder_layer(n, l, att, layer, taps[f"enc.{layer - 1}"])
+    for layer in (0, 1, 3, 27):
+        y = oracle.encoder_layer(n, l, att, layer, taps[f"enc.{layer - 1}" if layer else "embed"])
         assert np.array_equal(y.ravel(), taps[f"enc.{layer}"]), layer
 
 
-def test_encoder_layer_rejects_layer_zero(oracle):
-    with pytest.raises(RuntimeError):
-        oracle.encoder_layer(1, 4, np.ones(4, np.int64), 0, np.zeros((4, 1024), np.float32))
+def test_encoder_layer_rejects_a_layer_out_of_range(oracle):
+    for layer in (-1, 28):
+        with pytest.raises(RuntimeError):
+            oracle.encoder_layer(1, 4, np.ones(4, np.int64), layer, np.zeros((4, 1024), np.float32))
