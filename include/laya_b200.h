@@ -157,10 +157,15 @@ int laya_decision_tail_static(laya_engine *e, const float *x, int n, int k, cons
  * (tile_n 256 or 128); N % tile_n == 0, K % 64 == 0. */
 int laya_selftest_gemm(int device, const uint16_t *a, const uint16_t *w, float *out, int m,
                        int n, int k, int tile_n);
-/* Times the GEMM alone: random f16 operands on the device, `iters` launches
- * of out[M,N] (f32) = A . W^T on 256 x tile_n tiles; *ms = mean device time
- * per launch (CUDA events). */
-int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int iters, float *ms);
+/* Times the GEMM alone with one of the forward's epilogues: f16 operands of
+ * a fixed pattern on the device, `iters` launches of epi(A[M,K] . W[N,K]^T)
+ * on 256 x tile_n tiles, each bracketed by CUDA events; with flush_l2 != 0 a
+ * 256 MiB memset runs (untimed) before every launch so operands start cold.
+ * epi: 0 QKV + RoPE (n = 3072, f16 out), 1 QKV + bias, 2 residual add into
+ * f32 [M,N], 3 GeGLU (n = gate/up co-tiled columns, f16 out [M, n/2]),
+ * 4 bias + ReLU, 6 f32 store; tile_n 128 only for 2 and 6.
+ * *ms = mean device time per launch. */
+int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int epi, int flush_l2, int iters, float *ms);
 
 /* Ragged attention on qkv [R,3072] f16 (q,k pre-scaled) for sequences packed
  * back to back with lengths lens[n]; window < 0 for global.  out [R,1024] f32.

@@ -181,12 +181,14 @@ __global__ void __launch_bounds__(THREADS, Layout<kSingle>::MIN_BLOCKS)
   const int r = q0 + tid;  // this thread's query position
   const int xq = h * D, xk = 1024 + h * D, xv = 2048 + h * D;
 
+  // q/k/v tiles are read by this layer's attention only: evict-first
+  const uint64_t pol = l2_evict_first();
   auto load_kv = [&](int kb, bool with_q, bool with_v) {
     if (tid == 0) {
       mbar_arrive_expect_tx(c.kv_bar, TILE_BYTES * (1 + (with_q ? 1 : 0) + (with_v ? 1 : 0)));
-      if (with_q) tma_load_2d(sQ, &tm_qkv, xq, row_base + q0, c.kv_bar);
-      tma_load_2d(sK, &tm_qkv, xk, row_base + kb * TK, c.kv_bar);
-      if (with_v) tma_load_2d(sV, &tm_qkv, xv, row_base + kb * TK, c.kv_bar);
+      if (with_q) tma_load_2d_hint(sQ, &tm_qkv, xq, row_base + q0, c.kv_bar, pol);
+      tma_load_2d_hint(sK, &tm_qkv, xk, row_base + kb * TK, c.kv_bar, pol);
+      if (with_v) tma_load_2d_hint(sV, &tm_qkv, xv, row_base + kb * TK, c.kv_bar, pol);
     }
   };
   auto mma_s = [&]() {

@@ -1368,53 +1368,78 @@ int laya_selftest_gemm(int device, const uint16_t* a, const uint16_t* wt, float*
   });
 }
 
-int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int iters, float* ms) {
+int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int epi, int flush_l2, int iters, float* ms) {
   return guard([&] {
-    if (!ms || m <= 0 || n <= 0 || k <= 0 || iters <= 0 || (tile_n != laya::kGemmBN && tile_n != laya::kGemmBNNarrow) ||
-        n % tile_n || k % laya::kGemmBK)
-      throw Error(LAYA_E_INVALID, "bench_gemm: bad shape");
-    laya::ck(cudaSetDevice(device), "cudaSetDevice");
+    using namespace laya;
+    const bool epi_ok = epi == kEpiQkvRope || epi == kEpiQkvBias || epi == kEpiResid || epi == kEpiGeglu ||
+                        epi == kEpiBiasRelu || epi == kEpiStoreF32;
+    if (!ms || m <= 0 || n <= 0 || k <= 0 || iters <= 0 || !epi_ok || (tile_n != kGemmBN && tile_n != kGemmBNNarrow) ||
+        n % tile_n || k % kGemmBK || ((epi == kEpiQkvRope || epi == kEpiQkvBias) && n != 3 * H) ||
+        (tile_n != kGemmBN && epi != kEpiResid && epi != kEpiStoreF32))
+      throw Error(LAYA_E_INVALID, "bench_gemm: bad shape or epilogue");
+    ck(cudaSetDevice(device), "cudaSetDevice");
     int sms = 0;
-    laya::ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "attr");
-    laya::DevBuf da, dw, dout, derr;
+    ck(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device), "attr");
+    const bool f32_out = epi == kEpiResid || epi == kEpiStoreF32;
+    const int out_cols = epi == kEpiGeglu ? n / 2 : n;
+    DevBuf da, dw, dout, derr, dpos, dcos, dsin, dbias, dflush;
     da.alloc((size_t)m * k * 2, "a");
     dw.alloc((size_t)n * k * 2, "w");
-    dout.alloc((size_t)m * n * 4, "out");
+    dout.alloc((size_t)m * out_cols * (f32_out ? 4 : 2), "out");
     derr.alloc(256, "err");
-    // operands: a fixed small-integer pattern (exact in f16), no host copies
-    laya::ck(cudaMemset(da.p, 0x3c, da.bytes), "memset");
-    laya::ck(cudaMemset(dw.p, 0x2c, dw.bytes), "memset");
-    laya::ck(cudaMemset(derr.p, 0, 256), "memset");
+    dpos.alloc((size_t)m * 4, "pos");
+    dcos.alloc(128 * 32 * 4, "cos");
+    dsin.alloc(128 * 32 * 4, "sin");
+    dbias.alloc((size_t)n * 4, "bias");
+    // operands: a fixed pattern (f16 1.0039 and 0.0655), no host copies
+    ck(cudaMemset(da.p, 0x3c, da.bytes), "memset");
+    ck(cudaMemset(dw.p, 0x2c, dw.bytes), "memset");
+    ck(cudaMemset(dout.p, 0, dout.bytes), "memset");
+    ck(cudaMemset(derr.p, 0, 256), "memset");
+    ck(cudaMemset(dpos.p, 0, dpos.bytes), "memset");  // position 0 for every row
+    ck(cudaMemset(dcos.p, 0, dcos.bytes), "memset");
+    ck(cudaMemset(dsin.p, 0, dsin.bytes), "memset");
+    ck(cudaMemset(dbias.p, 0, dbias.bytes), "memset");
+    if (flush_l2) dflush.alloc((size_t)256 << 20, "l2 flush");
     CUtensorMap ta, tw, to;
-    if (laya::make_tmap_f16(&ta, da.p, m, k, laya::kGemmABoxRows) || laya::make_tmap_f16(&tw, dw.p, n, k, tile_n / 2) ||
-        laya::make_tmap_2d(&to, dout.p, true, m, n, 32, laya::kGemmOutBoxRows))
+    if (make_tmap_f16(&ta, da.p, m, k, kGemmABoxRows) || make_tmap_f16(&tw, dw.p, n, k, tile_n / 2) ||
+        make_tmap_2d(&to, dout.p, f32_out, m, out_cols, f32_out ? 32 : 64, kGemmOutBoxRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed");
-    laya::GemmArgs g{};
+    GemmArgs g{};
     g.M = m;
     g.N = n;
     g.K = k;
     g.err = derr.as<int>();
     g.out = dout.p;
-    g.ldo = n;
-    const laya::GemmMaps maps{&ta, &tw, &to};
-    for (int i = 0; i < 3; ++i)
-      laya::ck(laya::launch_gemm(laya::kEpiStoreF32, maps, g, sms, 0, tile_n), "gemm launch");
-    cudaEvent_t e0, e1;
-    laya::ck(cudaEventCreate(&e0), "event");
-    laya::ck(cudaEventCreate(&e1), "event");
-    laya::ck(cudaEventRecord(e0, 0), "event");
-    for (int i = 0; i < iters; ++i)
-      laya::ck(laya::launch_gemm(laya::kEpiStoreF32, maps, g, sms, 0, tile_n), "gemm launch");
-    laya::ck(cudaEventRecord(e1, 0), "event");
-    laya::ck(cudaEventSynchronize(e1), "sync");
-    float t = 0;
-    laya::ck(cudaEventElapsedTime(&t, e0, e1), "elapsed");
-    cudaEventDestroy(e0);
-    cudaEventDestroy(e1);
-    int ev = 0;
-    laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
-    if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("gemm device wait expired (code %d)", ev));
-    *ms = t / iters;
+    g.ldo = out_cols;
+    g.pos = dpos.as<int>();
+    g.cosb = dcos.as<float>();
+    g.sinb = dsin.as<float>();
+    g.scale = 0.125f;
+    g.bias = (epi == kEpiQkvBias || epi == kEpiBiasRelu) ? dbias.as<float>() : nullptr;
+    g.n_valid = out_cols;
+    const GemmMaps maps{&ta, &tw, &to};
+    for (int i = 0; i < 3; ++i) ck(launch_gemm(epi, maps, g, sms, 0, tile_n), "gemm launch");
+    std::vector<cudaEvent_t> ev(2 * (size_t)iters);
+    for (auto& e : ev) ck(cudaEventCreate(&e), "event");
+    for (int i = 0; i < iters; ++i) {
+      if (flush_l2) ck(cudaMemsetAsync(dflush.p, i & 0xff, dflush.bytes, 0), "flush");
+      ck(cudaEventRecord(ev[2 * i], 0), "event");
+      ck(launch_gemm(epi, maps, g, sms, 0, tile_n), "gemm launch");
+      ck(cudaEventRecord(ev[2 * i + 1], 0), "event");
+    }
+    ck(cudaEventSynchronize(ev.back()), "sync");
+    float total = 0;
+    for (int i = 0; i < iters; ++i) {
+      float t = 0;
+      ck(cudaEventElapsedTime(&t, ev[2 * i], ev[2 * i + 1]), "elapsed");
+      total += t;
+    }
+    for (auto e : ev) cudaEventDestroy(e);
+    int errv = 0;
+    ck(cudaMemcpy(&errv, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
+    if (errv) throw Error(LAYA_E_DEVICE_TIMEOUT, fmt("gemm device wait expired (code %d)", errv));
+    *ms = total / iters;
   });
 }
 

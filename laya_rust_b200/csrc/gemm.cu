@@ -105,6 +105,16 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// The same with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* smem_dst, const CUtensorMap* m, int x, int y,
+                                                      uint32_t bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* smem_src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(m)),
@@ -112,10 +122,13 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* s
                : "memory");
 }
 
+// Reduce-add into the f32 residual stream, which is kept in L2 (evict-last).
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* m, const void* smem_src, int x, int y) {
   asm volatile(
-      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
-          reinterpret_cast<uint64_t>(m)),
+      "{\n\t.reg .b64 pol;\n\t"
+      "createpolicy.fractional.L2::evict_last.b64 pol, 1.0;\n\t"
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group.L2::cache_hint"
+      " [%0, {%2, %3}], [%1], pol;\n\t}" ::"l"(reinterpret_cast<uint64_t>(m)),
       "r"(smem_u32(smem_src)), "r"(x), "r"(y)
       : "memory");
 }
@@ -370,6 +383,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   const bool leader = rank == 0;
   const int cluster_id = blockIdx.x >> 1;
   const int num_clusters = gridDim.x >> 1;
+  // tile t covers row block t / num_n and column tile t % num_n: the
+  // clusters running at one time share a few A row blocks
   const int num_m = (args.M + BM - 1) / BM;
   const int num_n = args.N / BN;
   const int num_tiles = num_m * num_n;
@@ -411,9 +426,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      // the A operand is read by the num_n clusters working on its row block
+      // at about the same time, and not after: evict-first
+      const uint64_t pol_a = l2_evict_first();
       for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
-        const int m0 = (tile % num_m) * BM + static_cast<int>(rank) * CTA_ROWS;
-        const int n0 = (tile / num_m) * BN + static_cast<int>(rank) * (BN / 2);
+        const int m0 = (tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
+        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag)) {
             ok = false;
@@ -421,7 +439,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t fb = map_to_rank(smem_u32(&full[stage]), 0);
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * C::STAGE_BYTES);
-          tma_load_2d_pair(sA + stage * C::A_BYTES, &tmA, kb * BK, m0, fb);
+          tma_load_2d_pair_hint(sA + stage * C::A_BYTES, &tmA, kb * BK, m0, fb, pol_a);
           tma_load_2d_pair(sB + stage * C::B_BYTES, &tmB, kb * BK, n0, fb);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -492,8 +510,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();
-      const int m0 = (tile % num_m) * BM + static_cast<int>(rank) * CTA_ROWS;
-      const int n0 = (tile / num_m) * BN;
+      const int m0 = (tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
+      const int n0 = (tile % num_n) * BN;
       const int row0 = m0 + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       st.active = row0 < args.M;

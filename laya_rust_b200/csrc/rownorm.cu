@@ -42,12 +42,18 @@ __device__ __forceinline__ void normalize(float (&v)[32], float eps) {
   for (int i = 0; i < 32; ++i) v[i] = (v[i] - mean) * rstd;
 }
 
-// element index of v[4*i + j] held by `lane`: i*128 + lane*4 + j
+// element index of v[4*i + j] held by `lane`: i*128 + lane*4 + j.  The rows
+// are the residual stream, kept in L2 (evict-last) between the kernels that
+// update and normalise it.
 __device__ __forceinline__ void load_f32(const float* row, int lane, float (&v)[32]) {
   const float4* p = reinterpret_cast<const float4*>(row);
+  const uint64_t pol = l2_evict_last();
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const float4 f = p[i * 32 + lane];
+    float4 f;
+    asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                 : "l"(p + i * 32 + lane), "l"(pol));
     v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
   }
 }
