@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(THREADS, Layout<kSingle>::MIN_BLOCKS)
     rr.lo = r - window > 0 ? r - window : 0;
     rr.hi = r + window + 1 < len ? r + window + 1 : len;
   }
+  if (r >= len) rr.hi = rr.lo;  // a row past the sequence: never stored, no scores
 
   // This row of S is streamed from TMEM one 32-key chunk at a time (a
   // second read is cheaper than holding 128 scores in registers).
