@@ -29,6 +29,7 @@ import numpy as np
 
 from . import arch
 from . import gguf
+from . import tokgen
 
 THETA_FULL = 160000.0
 THETA_SLIDING = 10000.0
@@ -85,6 +86,13 @@ def write_model(path: str, seed: int = 0, std: float = 0.02) -> str:
     for i in range(3):
         w.add_kv(f"laya.temperature.{i}", V(gguf.F32, 1.0))
     w.add_kv("laya.temperature_by_options", V(gguf.STR, "{}"))
+    # the tokenizer travels inside the model file, as the reference's
+    # converter embeds it (convert.rs:188-223; read back by lib.rs:47-57)
+    w.add_kv("tokenizer.ggml.model", V(gguf.STR, "gpt2"))
+    for key, name in (("bos", "[CLS]"), ("eos", "[SEP]"), ("cls", "[CLS]"), ("mask", "[MASK]"),
+                      ("unknown", "[UNK]"), ("padding", "[PAD]")):
+        w.add_kv(f"tokenizer.ggml.{key}_token_id", V(gguf.U32, dict((c, i) for c, i, _ in tokgen.SPECIALS)[name]))
+    w.add_kv("tokenizer.huggingface.json", V(gguf.STR, tokgen.tokenizer_json(seed)))
     for name in arch.weight_names():
         shape = shapes[name]
         gdims = list(reversed(shape))
@@ -110,7 +118,7 @@ def cached_model(seed: int = 0, std: float = 0.02, directory: str | None = None)
     (default: ``$LAYA_MODEL_CACHE`` or ``/tmp/laya-b200-models``)."""
     directory = directory or os.environ.get("LAYA_MODEL_CACHE", "/tmp/laya-b200-models")
     os.makedirs(directory, exist_ok=True)
-    tag = hashlib.sha1(f"v1:{seed}:{std}".encode()).hexdigest()[:10]
+    tag = hashlib.sha1(f"v3:{seed}:{std}".encode()).hexdigest()[:10]
     path = os.path.join(directory, f"laya-rand-s{seed}-{tag}.gguf")
     if not os.path.exists(path):
         write_model(path, seed=seed, std=std)

@@ -177,6 +177,77 @@ def pack_stream(requests, max_tokens: int = 16384):
     return forwards
 
 
+# ---- System One requests as JSON text (through the C++ front end) ------------------
+# Words are the letter-only entries of the model's tokenizer vocabulary (a
+# space-prefixed entry "Gword" stands for " word"), drawn uniformly, so the
+# text tokenizes to about one token per word as real text does with a real
+# vocabulary.
+
+def vocab_words(tokenizer_json: str) -> list[str]:
+    import json as _json
+    from .tokgen import bytes_to_unicode
+    inv = {c: b for b, c in bytes_to_unicode().items()}
+    words = []
+    for tok in _json.loads(tokenizer_json)["model"]["vocab"]:
+        try:
+            text = bytes(inv[c] for c in tok).decode("ascii")
+        except (KeyError, UnicodeDecodeError):
+            continue
+        if text.startswith(" ") and len(text) > 2 and text[1:].isalpha():
+            words.append(text[1:])
+    return sorted(set(words))
+
+
+def _text(rng, words, n) -> str:
+    return " ".join(words[int(i)] for i in rng.integers(0, len(words), int(n)))
+
+
+def random_questions(rng) -> list:
+    """Config 4's question mix: 1..16 questions, choice (2..6 criteria of 3..8
+    words) and noul 1:1, instructions 8..16 words."""
+    qs = []
+    for _ in range(int(rng.integers(1, 17))):
+        instr = int(rng.integers(8, 17))
+        if rng.random() < 0.5:
+            qs.append(("choice", [int(c) for c in rng.integers(3, 9, int(rng.integers(2, 7)))], instr))
+        else:
+            qs.append(("noul", instr))
+    return qs
+
+
+def system_one_request_json(rng, words, state_words, questions) -> dict:
+    """A request object as the reference's API takes it (systemone.rs:74-118):
+    {"state": text, "questions": {id: {"type", "instructions", "criteria"}}}."""
+    qs = {}
+    for i, q in enumerate(questions):
+        if q[0] == "choice":
+            crit = {}
+            for j, c in enumerate(q[1]):
+                crit[f"{words[int(rng.integers(0, len(words)))]}_{j}"] = _text(rng, words, max(1, c - 1))
+            qs[f"q{i}"] = {"type": "choice", "instructions": _text(rng, words, q[2]), "criteria": crit}
+        else:
+            qs[f"q{i}"] = {"type": "noul", "instructions": _text(rng, words, q[1])}
+    return {"state": _text(rng, words, state_words), "questions": qs}
+
+
+def single_request_json(words, seed: int = 0) -> dict:
+    """Config 0 as request JSON: a 48-word state, a choice question with 2
+    criteria of 6 words, a noul question with 12-word instructions."""
+    rng = np.random.default_rng(seed)
+    return system_one_request_json(rng, words, 48, [("choice", [6, 6], 8), ("noul", 12)])
+
+
+def request_stream_json(words, n_requests: int = 4096, seed: int = 4) -> list[dict]:
+    """Config 4 as request JSON: state length lognormal (median 96 words,
+    sigma 0.8, capped at 1024), questions as random_questions."""
+    rng = np.random.default_rng(seed)
+    out = []
+    for _ in range(n_requests):
+        state = int(min(1024, round(float(rng.lognormal(np.log(96.0), 0.8)))))
+        out.append(system_one_request_json(rng, words, max(1, state), random_questions(rng)))
+    return out
+
+
 def real_tokens(req: Req) -> int:
     return int((req.att != 0).sum())
 

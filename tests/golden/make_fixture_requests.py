@@ -1,13 +1,22 @@
-"""Extracts the request layout of the reference's golden fixtures.
+"""Extracts the reference's golden fixtures for the tests.
 
-Reads laya-rust ``tests/fixtures/*.json`` (recorded by the reference's ``golden``
-command with ``--max-tokens 300``) and keeps only what does not depend on the
-real checkpoint: per forward the padded index arrays (ids, att, mpos, mmask,
-qtype), the question ids of each row, and the request's question order.  The
-logits/act/answers in those files need the real weights and are dropped.
+Reads laya-rust ``tests/fixtures/*.json`` (recorded by the reference's
+``golden`` command with ``--max-tokens 300``) and ``tests/scenarios.json``.
+
+``fixture_requests.json``: per fixture the padded index arrays of each
+forward (ids, att, mpos, mmask, qtype), the question ids of each row and the
+request's question order -- the request layout, which does not depend on the
+real checkpoint.
+
+``fixture_outputs.json``: per fixture the request JSON (key order kept), each
+forward's rows with the reference's recorded logits and act, and the answers
+object the reference computed from them.  Logits and act come from the real
+checkpoint, but the scoring that turns them into answers (score_row,
+softmax_t, confidence, answer; main.rs:502-518, systemone.rs:200-296) does
+not, so these pin the front end's scoring and number formatting.  Also the
+scenario requests of scenarios.json.
 
 Usage: python tests/golden/make_fixture_requests.py <reference-root>
-Writes tests/golden/fixture_requests.json.
 """
 import glob
 import json
@@ -31,6 +40,24 @@ def main(ref_root: str) -> None:
     with open(dst, "w") as f:
         json.dump(out, f, separators=(",", ":"))
     print(dst, len(out), "fixtures")
+
+    outs = []
+    for path in sorted(glob.glob(os.path.join(ref_root, "tests", "fixtures", "*.json"))):
+        text = open(path).read()
+        d = json.loads(text)
+        # the answers with every float kept as the literal text the reference
+        # printed (serde_json / ryu), to pin the number formatting too
+        raw = json.loads(text, parse_float=lambda t: {"f64": t})["answers"]
+        outs.append({"name": d["name"], "request": d["request"],
+                     "forwards": [{"rows": fw["rows"], "k": fw["k"], "logits": fw["logits"], "act": fw["act"]}
+                                  for fw in d["forwards"]],
+                     "answers": d["answers"], "answers_literal": raw})
+    scen = json.load(open(os.path.join(ref_root, "tests", "scenarios.json")))
+    dst = os.path.join(os.path.dirname(os.path.abspath(__file__)), "fixture_outputs.json")
+    with open(dst, "w") as f:
+        json.dump({"fixtures": outs, "scenarios": [{"name": s["name"], "request": s["request"]}
+                                                   for s in scen["scenarios"]]}, f, separators=(",", ":"))
+    print(dst, len(outs), "fixtures,", len(scen["scenarios"]), "scenarios")
 
 
 if __name__ == "__main__":

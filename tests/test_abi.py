@@ -10,13 +10,15 @@ import pytest
 from laya_rust_b200 import engine as E
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADER = os.path.join(ROOT, "include", "laya_b200.h")
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("laya_b200.h", "laya_frontend.h")]
 
 
 def declared_functions():
-    text = open(HEADER).read()
-    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"\b(laya_[a-z0-9_]+)\s*\(", text)) - {"laya_tap_fn"})
+    names = set()
+    for h in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", open(h).read(), flags=re.S)
+        names |= set(re.findall(r"\b(laya_[a-z0-9_]+)\s*\(", text))
+    return sorted(names - {"laya_tap_fn"})
 
 
 def test_header_declares_the_engine_seam():
