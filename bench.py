@@ -13,13 +13,15 @@ Workloads (--config), all seeded synthetic data on a random-init f16 model:
                256 (real lengths U[16,256]), f16 N(0,1) activations; global
                layer 0 and local layer 1 timed separately, L2 flushed before
                every step (the layer's weights and activations fit in L2).
-  request      config 0: one System One request (48-word state, a choice
-               question with 2 criteria, a noul question) through the request
-               path (group_by_budget, build_batch, forward, scoring); the
-               metric is its latency (ms, p50 over the steps).
-  stream       config 4: 4096 seeded requests assigned to the GPUs greedily by
-               token cost; each GPU packs its share into <=16384-token
-               forwards.  Steps are the forwards of one pass over the stream.
+  request      config 0: one System One request (JSON: 48-word state, a
+               choice question with 2 criteria, a noul question) through the
+               C++ front end (planned once; per step group_by_budget,
+               build_batch, forward, scoring, response JSON); the metric is
+               its latency (ms, p50 over the steps).
+  stream       config 4: 4096 seeded JSON requests planned by the C++ front end
+               on the host threads, assigned to the GPUs greedily by token
+               cost; each GPU packs its share across requests into
+               <=16384-token forwards.  Steps are the forwards of one pass.
 
   value     device-resident: requests uploaded once (plans), forwards
             enqueued back to back (CUDA graph replay where one plan repeats);
@@ -137,22 +139,6 @@ def oracle_model():
     return OracleModel(modelgen.cached_model(seed=0))
 
 
-class OracleEngine:
-    """The oracle behind the Engine.forward call, so the request path
-    (batching.run_all) can run on the reference CPU algorithm."""
-
-    def __init__(self):
-        self.m = oracle_model()
-
-    def forward(self, req):
-        from laya_rust_b200.engine import Out
-        lg, act = self.m.forward(req.n, req.l, req.k, req.ids, req.att, req.mpos, req.mmask, req.qtype)
-        return Out(req.n, req.k, lg, act)
-
-    def close(self):
-        self.m.close()
-
-
 def cpu_run(req, steps, warmup):
     """Times the oracle (the reference CPU algorithm) on `req`; returns seconds per step."""
     m = oracle_model()
@@ -183,24 +169,39 @@ def cpu_layer_run(req, steps, warmup):
     return statistics.mean(times)
 
 
-def cpu_request_run(items, steps, warmup):
-    """Times the request path on the oracle; returns per-run milliseconds."""
-    from laya_rust_b200 import batching
-    eng = OracleEngine()
-    times = []
+def cpu_request_run(requests, steps, warmup):
+    """Times run_all (main.rs:520-557) of each request on the reference CPU
+    algorithm: the restated front end (oracle/frontend_ref.py) planning,
+    batching and scoring around the C oracle's forward.  Returns per-step
+    milliseconds and the tokens of one step."""
+    from laya_rust_b200 import tokgen
+    from oracle import frontend_ref as F
+    tok = F.Tokenizer(tokgen.tokenizer_json(0))
+    m = oracle_model()
+    times, toks = [], 0
     for i in range(warmup + steps):
         t0 = time.perf_counter()
-        batching.run_all(eng, items)
+        toks = 0
+        for req in requests:
+            out = F.run_all(m.forward, tok, req)
+            toks += out["usage"]["input_tokens"]
         if i >= warmup:
             times.append((time.perf_counter() - t0) * 1e3)
-    eng.close()
-    return times
+    m.close()
+    return times, toks
+
+
+def request_words():
+    from laya_rust_b200 import tokgen, workloads
+    return workloads.vocab_words(tokgen.tokenizer_json(0))
 
 
 def stream_sample():
-    """The CPU sample of the stream: the first 4 questions of request 0."""
+    """The CPU sample of the stream: request 0 with its first 4 questions."""
     from laya_rust_b200 import workloads
-    return workloads.request_stream(1, 4)[0][:4]
+    req = workloads.request_stream_json(request_words(), 1, 4)[0]
+    keep = list(req["questions"])[:4]
+    return {"state": req["state"], "questions": {k: req["questions"][k] for k in keep}}
 
 
 class ClockSampler:
@@ -290,17 +291,18 @@ def run_reference(args):
                       f"{sample.n * sample.l} padded tokens), {what} per step; {note}")
         line = base_line(args, METRIC, v, UNIT, args.gpus, sec * 1e3, cfg, dtype="f32", impl="reference")
     else:
-        items = workloads.single_request(0) if args.config == "request" else stream_sample()
-        times = cpu_request_run(items, args.steps, args.warmup)
+        req = workloads.single_request_json(request_words(), 0) if args.config == "request" else stream_sample()
+        times, toks = cpu_request_run([req], args.steps, args.warmup)
         lat = latency_summary(times)
-        toks = sum(len(i.seq) for i in items)
+        nq = len(req["questions"])
         if args.config == "request":
             v, unit, metric, hib = lat["p50"], "ms", LAT_METRIC, False
         else:
             v, unit, metric, hib = toks / (lat["mean"] / 1e3), UNIT, METRIC, True
-        cfg = {"workload": args.config, "model": MODEL, "questions": len(items), "real_tokens": toks}
-        sample_txt = (f"{'the request' if args.config == 'request' else 'first 4 questions of request 0'} "
-                      f"({len(items)} questions, {toks} tokens) through run_all per step; {note}")
+        cfg = {"workload": args.config, "model": MODEL, "questions": nq, "real_tokens": toks}
+        sample_txt = (f"{'the request' if args.config == 'request' else 'request 0 with its first 4 questions'} "
+                      f"({nq} questions, {toks} tokens) through run_all (restated front end + C oracle forward) "
+                      f"per step; {note}")
         line = base_line(args, metric, v, unit, args.gpus, lat["mean"], cfg, hib=hib, dtype="f32",
                          impl="reference", latency_ms=lat)
     line["cpu_baseline"] = {"value": line["value"], "unit": line["unit"], "cores": cores, "kind": "port",
@@ -570,16 +572,28 @@ def run_layer(args, d, eng):
 
 
 def run_request(args, d, eng):
-    """Config 0: latency of one System One request through the request path."""
-    from laya_rust_b200 import batching, workloads
+    """Config 0: one System One request (JSON) through the C++ front end and
+    the engine.  As the reference's bench (main.rs:661-694: prepare once,
+    then time run_all), the request is planned (parsed, tokenized, laid out)
+    once; each step packs it (group_by_budget), builds the batches, runs
+    laya_forward per forward, scores and writes the response JSON.  The
+    planning time is reported beside it."""
+    from laya_rust_b200 import frontend as FE, modelgen, workloads
     torch = d.torch
-    items = workloads.single_request(0)
-    groups = batching.group_by_budget(items, 16384)
-    reqs = [batching.build_batch(items, g) for g in groups]
-    toks = sum(len(i.seq) for i in items)
+    tok = FE.Tokenizer(gguf_path=modelgen.cached_model(seed=0))
+    req = workloads.single_request_json(request_words(), 0)
+    plan_ms = []
+    for _ in range(max(args.steps, 5)):
+        t = time.perf_counter()
+        FE.Requests(tok, [req], threads=1).close()
+        plan_ms.append((time.perf_counter() - t) * 1e3)
+    rq = FE.Requests(tok, [req], threads=1)
+    nf = rq.pack(16384, False)
+    batches = [rq.batch(f) for f in range(nf)]
+    toks = sum(int(b.att.sum()) for b in batches)
 
     # device time of the request's forwards (plans replayed as graphs)
-    plans = [eng.plan(r) for r in reqs]
+    plans = [eng.plan(b) for b in batches]
     for p in plans:
         p.capture()
     stream = ext_stream(d, eng)
@@ -602,47 +616,80 @@ def run_request(args, d, eng):
     for p in plans:
         p.close()
 
+    def run_all():
+        for f in range(rq.pack(16384, False)):
+            out = eng.forward(rq.batch(f))
+            rq.score(f, out.logits, out.act)
+        return rq.response_text(0)
+
     clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
     for _ in range(args.warmup):
-        batching.run_all(eng, items)
+        run_all()
     d.barrier()
     times = []
     for _ in range(args.steps):
         e0 = time.perf_counter()
-        batching.run_all(eng, items)
+        resp = run_all()
         times.append((time.perf_counter() - e0) * 1e3)
     clk = clocks.stop() if clocks else None
+    assert json.loads(resp)["usage"]["input_tokens"] == toks
     lat = latency_summary(times)
     p50 = d.allmax(lat["p50"])
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
-        ct = cpu_request_run(items, 1, 0)
-        cpu = cpu_baseline_line(ct[0], "ms", f"the same request ({len(items)} questions, {toks} tokens), one run")
+        ct, _ = cpu_request_run([req], 1, 0)
+        cpu = cpu_baseline_line(ct[0], "ms", f"the same request ({len(req['questions'])} questions, {toks} tokens) "
+                                             "through run_all (restated front end + C oracle forward), one run")
     if d.rank == 0:
-        cfg = {"workload": "request", "model": MODEL, "questions": len(items), "forwards": len(reqs),
-               "real_tokens": toks, "seq_lens": [len(i.seq) for i in items],
-               "markers": [len(i.markers) for i in items], "parallelism": f"replicas{d.world}",
-               "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
+        cfg = {"workload": "request", "model": MODEL, "questions": len(req["questions"]), "forwards": nf,
+               "real_tokens": toks, "seq_lens": [int(x) for b in batches for x in b.att.reshape(b.n, b.l).sum(1)],
+               "parallelism": f"replicas{d.world}", "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
         e2e = {"value": p50, "unit": "ms", "h2d_bytes_per_step": upload,
-               "d2h_bytes_per_step": sum(4 * (r.n * r.k + 2 * r.n) for r in reqs),
-               "path": "batching.run_all -> laya_forward per forward group, scoring on host"}
+               "d2h_bytes_per_step": sum(4 * (b.n * b.k + 2 * b.n) for b in batches),
+               "path": "C++ front end (pack, build_batch) -> laya_forward per forward -> score -> response JSON"}
         line = base_line(args, LAT_METRIC, p50, "ms", d.world, lat["mean"], cfg, hib=False,
                          latency_ms=lat, device_ms_per_request=dev_ms,
+                         frontend_plan_ms=statistics.median(plan_ms),
                          tokens_per_s=toks / (lat["mean"] / 1e3), e2e=e2e,
                          gpu_launches=launches * args.steps, clocks=clk, cpu_baseline=cpu)
         print(json.dumps(line), flush=True)
+    rq.close()
+    tok.close()
 
 
 def run_stream(args, d, eng):
-    """Config 4: the request stream, assigned greedily by cost, packed per GPU."""
+    """Config 4: the request stream (JSON) through the C++ front end: every
+    rank plans all requests on its host threads to learn their token costs,
+    takes the share the greedy cost assignment gives it, and packs its
+    questions across requests into <=16384-token forwards."""
     import numpy as np
-    from laya_rust_b200 import batching, workloads
+    from laya_rust_b200 import frontend as FE, modelgen, workloads
     torch = d.torch
-    reqs = workloads.request_stream(args.requests, 4)
-    mine = workloads.assign_requests(reqs, d.world)[d.rank]
-    fws = workloads.pack_stream([reqs[i] for i in mine])
-    batches = [batching.build_batch(items, list(range(len(items)))) for items, _ in fws]
+    tok = FE.Tokenizer(gguf_path=modelgen.cached_model(seed=0))
+    texts = [json.dumps(r) for r in workloads.request_stream_json(request_words(), args.requests, 4)]
+    t = time.perf_counter()
+    allq = FE.Requests(tok, texts, threads=0)
+    plan_all_s = time.perf_counter() - t
+    cost = [0] * len(texts)
+    for i in range(allq.questions()):
+        r, ln, _, _ = allq.question_shape(i)
+        cost[r] += ln
+    allq.close()
+    load = [0] * d.world
+    mine = []
+    for r, c in enumerate(cost):   # greedy by token cost, in dispatch order
+        g = min(range(d.world), key=lambda w: (load[w], w))
+        load[g] += c
+        if g == d.rank:
+            mine.append(r)
+    t = time.perf_counter()
+    rq = FE.Requests(tok, [texts[i] for i in mine], threads=0)
+    plan_s = time.perf_counter() - t
+    nf = rq.pack(16384, True)
+    batches = [rq.batch(f) for f in range(nf)]
+    fq = [rq.forward_questions(f) for f in range(nf)]
+    q_req = [rq.question_shape(i)[0] for i in range(rq.questions())]
     plans = [eng.plan(b) for b in batches]
     real = sum(p.stats()[0] for p in plans)
     upload = sum(p.stats()[2] for p in plans)
@@ -673,25 +720,27 @@ def run_stream(args, d, eng):
     for p in plans:
         p.close()
 
-    # e2e: every forward through laya_forward, scored on the host; a request's
-    # service latency runs from the start of the forward holding its first
-    # question to the end of the one holding its last; its completion time is
-    # measured from the start of the pass (all requests queued at t = 0).
-    cal = batching.Calibration()
+    # e2e: every forward through laya_forward and the C++ scorer, then every
+    # response.  A request's service latency runs from the start of the
+    # forward holding its first question to the end of the one holding its
+    # last; its completion latency is measured from the start of the pass
+    # (all requests queued at t = 0).
     d.barrier()
     start = time.perf_counter()
     t_beg, t_end = [], []
-    for (items, ids), b in zip(fws, batches):
+    for f, b in enumerate(batches):
         t_beg.append(time.perf_counter() - start)
         out = eng.forward(b)
-        for row, it in enumerate(items):
-            batching.score_row(out.logits, out.act, row, b.k, len(it.markers), it.qtype, cal)
+        rq.score(f, out.logits, out.act)
         t_end.append(time.perf_counter() - start)
+    for r in range(len(mine)):
+        rq.response_text(r)
     e_sec = d.allmax(time.perf_counter() - start)
     clk = clocks.stop() if clocks else None
     first, last = {}, {}
-    for f, (_, ids) in enumerate(fws):
-        for r, _ in ids:
+    for f, qs in enumerate(fq):
+        for q in qs:
+            r = q_req[q]
             first.setdefault(r, f)
             last[r] = f
     service = [(t_end[last[r]] - t_beg[first[r]]) * 1e3 for r in first]
@@ -699,34 +748,39 @@ def run_stream(args, d, eng):
     all_service = [v for part in d.gather(service) for v in part]
     all_completion = [v for part in d.gather(completion) for v in part]
     total_real = d.allsum(real)
-    forwards = d.allsum(len(fws))
+    forwards = d.allsum(nf)
+    plan_tokens = d.allsum(real)
+    plan_s_max = d.allmax(plan_s)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
-        items = stream_sample()
-        ct = cpu_request_run(items, 1, 0)
-        toks = sum(len(i.seq) for i in items)
+        ct, toks = cpu_request_run([stream_sample()], 1, 0)
         cpu = cpu_baseline_line(toks / (ct[0] / 1e3), UNIT,
-                                f"first 4 questions of request 0 ({toks} tokens) through run_all, one run")
+                                f"request 0 with its first 4 questions ({toks} tokens) through run_all "
+                                "(restated front end + C oracle forward), one run")
     if d.rank == 0:
-        cfg = {"workload": "stream", "model": MODEL, "requests": len(reqs),
-               "questions": sum(len(r) for r in reqs), "forwards": int(forwards),
-               "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
+        cfg = {"workload": "stream", "model": MODEL, "requests": len(texts), "questions": int(d.allsum(rq.questions())),
+               "forwards": int(forwards), "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
                "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
                "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
-        steps = len(fws)
+        steps = nf
         e2e = {"value": total_real / e_sec, "unit": UNIT, "h2d_bytes_per_step": upload / steps,
                "d2h_bytes_per_step": sum(4 * (b.n * b.k + 2 * b.n) for b in batches) / steps,
                "makespan_s": e_sec, "service_latency_ms": latency_summary(all_service),
                "completion_latency_ms": latency_summary(all_completion),
-               "path": "laya_forward per packed forward, scoring on host"}
+               "path": "laya_forward per packed forward, C++ scoring and response JSON"}
+        frontend = {"plan_s": plan_s_max, "plan_tokens_per_s": plan_tokens / plan_s_max,
+                    "plan_all_requests_s": plan_all_s, "host_threads": os.cpu_count(),
+                    "what": "parse + tokenize + System One layout of the rank's requests on all host threads"}
         line = base_line(args, METRIC + " (request stream)", total_real / (ms_max / 1e3), UNIT, d.world,
                          ms_max / steps, cfg, padded_tokens_per_s=d.allsum(padded) / (ms_max / 1e3),
-                         device_makespan_s=ms_max / 1e3, e2e=e2e, gpu_launches=launches, clocks=clk,
-                         cpu_baseline=cpu)
+                         device_makespan_s=ms_max / 1e3, e2e=e2e, frontend=frontend, gpu_launches=launches,
+                         clocks=clk, cpu_baseline=cpu)
         line["steps"] = steps
         line["warmup"] = min(args.warmup, len(plans)) + len(big)
         print(json.dumps(line), flush=True)
+    rq.close()
+    tok.close()
 
 
 def run_b200(args):

@@ -78,6 +78,8 @@ int laya_requests_question_tokens(const laya_requests *r, int64_t i, int64_t *se
 int laya_requests_pack(laya_requests *r, int64_t max_tokens, int across_requests, int64_t *n_forwards);
 /* Forward f's batch shape. */
 int laya_requests_forward_shape(const laya_requests *r, int64_t f, int64_t *n, int64_t *l, int64_t *k);
+/* The question index of each of forward f's n rows. */
+int laya_requests_forward_questions(const laya_requests *r, int64_t f, int64_t *questions);
 /* build_batch (main.rs:470-500) into caller arrays: ids, att [n*l]; mpos,
  * mmask [n*k]; qtype [n] -- a laya_req's arrays. */
 int laya_requests_forward_batch(const laya_requests *r, int64_t f, int64_t *ids, int64_t *att, int64_t *mpos,

@@ -900,6 +900,15 @@ int laya_requests_forward_shape(const laya_requests* r, int64_t f, int64_t* n, i
   });
 }
 
+int laya_requests_forward_questions(const laya_requests* r, int64_t f, int64_t* questions) {
+  return guard([&] {
+    if (!r || !questions || f < 0 || f >= static_cast<int64_t>(r->r.forwards.size()))
+      throw Error(LAYA_E_INVALID, "forward out of range");
+    const auto& fw = r->r.forwards[f];
+    std::copy(fw.begin(), fw.end(), questions);
+  });
+}
+
 int laya_requests_forward_batch(const laya_requests* r, int64_t f, int64_t* ids, int64_t* att, int64_t* mpos,
                                 int64_t* mmask, int64_t* qtype) {
   return guard([&] {

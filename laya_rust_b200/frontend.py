@@ -42,6 +42,7 @@ def lib():
         L.laya_requests_pack.argtypes = [vp, ctypes.c_int64, ctypes.c_int, _i64p]
         L.laya_requests_forward_shape.argtypes = [vp, ctypes.c_int64, _i64p, _i64p, _i64p]
         L.laya_requests_forward_batch.argtypes = [vp, ctypes.c_int64, _i64p, _i64p, _i64p, _i64p, _i64p]
+        L.laya_requests_forward_questions.argtypes = [vp, ctypes.c_int64, _i64p]
         L.laya_requests_set_calibration.argtypes = [vp, _f32p, ctypes.c_char_p]
         L.laya_requests_score.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
         L.laya_requests_response.argtypes = [vp, ctypes.c_int64, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
@@ -124,6 +125,20 @@ class Requests:
         mk = np.empty(max(nm.value, 1), np.int64)
         _check(lib().laya_requests_question_tokens(self._h, i, _p64(seq), _p64(mk)))
         return {"request": req.value, "seq": seq.tolist(), "markers": mk[:nm.value].tolist(), "qtype": qt.value}
+
+    def question_shape(self, i: int) -> tuple[int, int, int, int]:
+        """(request, seq_len, markers, qtype) of question i."""
+        req, ln, nm, qt = (ctypes.c_int64() for _ in range(4))
+        _check(lib().laya_requests_question(self._h, i, ctypes.byref(req), ctypes.byref(ln), ctypes.byref(nm),
+                                            ctypes.byref(qt)))
+        return req.value, ln.value, nm.value, qt.value
+
+    def forward_questions(self, f: int) -> list[int]:
+        n = ctypes.c_int64()
+        _check(lib().laya_requests_forward_shape(self._h, f, ctypes.byref(n), None, None))
+        q = np.empty(max(n.value, 1), np.int64)
+        _check(lib().laya_requests_forward_questions(self._h, f, _p64(q)))
+        return q[:n.value].tolist()
 
     def pack(self, max_tokens: int = 16384, across_requests: bool = False) -> int:
         n = ctypes.c_int64()
