@@ -268,6 +268,33 @@ def base_line(args, metric, value, unit, n, ms_per_step, config, hib=True, **ext
 
 # ---- reference arm -------------------------------------------------------------------
 
+def reference_gpu_schedule(req, iters=3):
+    """The reference's GPU algorithm on this GPU, for context beside the CPU
+    arm: its own CUDA kernels (src/backend/cuda/kernels.rs) and cuBLAS FP32
+    op sequence (src/backend/cuda/mod.rs:466-812) on the full padded batch,
+    built into oracle/_ref/ from the reference tree.  None without a GPU or
+    without that build."""
+    try:
+        import torch
+        if not torch.cuda.is_available():
+            return None
+        from oracle import ref_gpu
+        if not ref_gpu.available():
+            return {"unavailable": "oracle/_ref/libref_gpu.so not built (needs the reference tree at build time)"}
+        from laya_rust_b200 import workloads
+        m = oracle_model()
+        rg = ref_gpu.RefGpuSchedule(m)
+        ms = rg.time(req.n, req.l, req.k, req.ids, req.att, req.mpos, req.mmask, req.qtype, iters)
+        rg.close()
+        m.close()
+        real = workloads.real_tokens(req)
+        return {"value": real / (ms / 1e3), "unit": UNIT, "ms_per_forward": ms, "iters": iters,
+                "what": "reference kernels + cuBLAS FP32 (default math) on the padded batch, device time per "
+                        "forward incl. its request copies"}
+    except Exception as e:  # a baseline for context only: never fail the arm
+        return {"unavailable": f"{type(e).__name__}: {e}"}
+
+
 def run_reference(args):
     rank, _, world = env_rank()
     if rank != 0:
@@ -307,6 +334,8 @@ def run_reference(args):
                          impl="reference", latency_ms=lat)
     line["cpu_baseline"] = {"value": line["value"], "unit": line["unit"], "cores": cores, "kind": "port",
                             "sample": sample_txt}
+    if args.config in ("forward-16k", "long-state"):
+        line["reference_gpu_schedule"] = reference_gpu_schedule(workload(args.config, 0))
     line["e2e"] = {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     print(json.dumps(line), flush=True)
 

@@ -649,6 +649,17 @@ static const lo_weight *W(const lo_model *m, const char *name) {
     abort();
 }
 
+/* A loaded weight's f32 data in graph layout, or NULL (for harnesses that
+ * copy the oracle's weights elsewhere). */
+const float *lo_weight_data(const lo_model *m, const char *name, size_t *count) {
+    for (int i = 0; i < m->nw; i++)
+        if (strcmp(m->w[i].name, name) == 0) {
+            if (count) *count = m->w[i].nd == 1 ? m->w[i].dims[0] : m->w[i].dims[0] * m->w[i].dims[1];
+            return m->w[i].data;
+        }
+    return NULL;
+}
+
 void lo_close(lo_model *m) {
     if (!m) return;
     for (int i = 0; i < m->nw; i++) free(m->w[i].data);

@@ -43,6 +43,8 @@ def lib():
         L.lo_forward_ex.restype = ctypes.c_int
         L.lo_forward_ex.argtypes = [ctypes.c_void_p, _sz, _sz, _sz, _i64p, _i64p, _i64p, _i64p,
                                     _i64p, _f32p, _f32p, TAP_FN, ctypes.c_void_p]
+        L.lo_weight_data.restype = ctypes.POINTER(ctypes.c_float)
+        L.lo_weight_data.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.POINTER(_sz)]
         L.lo_encoder_layer.restype = ctypes.c_int
         L.lo_encoder_layer.argtypes = [ctypes.c_void_p, _sz, _sz, _i64p, ctypes.c_int, _f32p]
         L.lo_f2h.restype = ctypes.c_uint16
