@@ -347,14 +347,20 @@ class Dist:
         import torch
         self.torch = torch
         self.rank, self.local, self.world = env_rank()
+        self.cuda = torch.cuda.is_available()
         if self.world > 1:
             import torch.distributed as dist
             from datetime import timedelta
-            torch.cuda.set_device(self.local)
-            dist.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                    device_id=torch.device("cuda", self.local))
+            # short: a rank that waits for a peer that never comes ends with an error
+            if self.cuda:
+                torch.cuda.set_device(self.local)
+                dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                        device_id=torch.device("cuda", self.local))
+            else:  # host-only runs (tests of the collective steps)
+                dist.init_process_group("gloo", timeout=timedelta(seconds=60))
             self.dist = dist
-        torch.cuda.set_device(self.local)
+        if self.cuda:
+            torch.cuda.set_device(self.local)
 
     def barrier(self):
         if self.world > 1:
@@ -363,7 +369,7 @@ class Dist:
     def _reduce(self, x, op):
         if self.world == 1:
             return x
-        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda")
+        t = self.torch.tensor([x], dtype=self.torch.float64, device="cuda" if self.cuda else "cpu")
         self.dist.all_reduce(t, op=op)
         return float(t.item())
 
@@ -584,12 +590,13 @@ def run_layer(args, d, eng):
         cpu = cpu_baseline_line(workloads.real_tokens(sample) / sec, UNIT,
                                 f"first {sample.n} sequences ({workloads.real_tokens(sample)} real / "
                                 f"{sample.n * sample.l} padded tokens), layers 0 and 1 once each")
+    padded_all = d.allsum(req.n * req.l)   # every rank takes the same collective steps
     if d.rank == 0:
         cfg = config_of(args, req, d.world)
         cfg["l2"] = "flushed (256 MiB memset) before every timed step"
         cfg["layers"] = {k: v for k, v in LAYERS}
         line = base_line(args, METRIC + " (one encoder layer)", value, UNIT, d.world, mean_ms, cfg,
-                         padded_tokens_per_s=d.allsum(req.n * req.l) / (mean_ms / 1e3), layers=per_kind,
+                         padded_tokens_per_s=padded_all / (mean_ms / 1e3), layers=per_kind,
                          roofline={"bound": "tensor", "kernel": "one encoder layer (4 tcgen05 GEMMs, attention, 2 norms)",
                                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                                    "peak_source": f"{pk_src} bf16_tflops (burst: a layer is timed alone)",
@@ -780,6 +787,8 @@ def run_stream(args, d, eng):
     forwards = d.allsum(nf)
     plan_tokens = d.allsum(real)
     plan_s_max = d.allmax(plan_s)
+    questions_all = d.allsum(rq.questions())   # every rank takes the same collective steps
+    padded_all = d.allsum(padded)
 
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
@@ -788,7 +797,7 @@ def run_stream(args, d, eng):
                                 f"request 0 with its first 4 questions ({toks} tokens) through run_all "
                                 "(restated front end + C oracle forward), one run")
     if d.rank == 0:
-        cfg = {"workload": "stream", "model": MODEL, "requests": len(texts), "questions": int(d.allsum(rq.questions())),
+        cfg = {"workload": "stream", "model": MODEL, "requests": len(texts), "questions": int(questions_all),
                "forwards": int(forwards), "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
                "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
                "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
@@ -802,7 +811,7 @@ def run_stream(args, d, eng):
                     "plan_all_requests_s": plan_all_s, "host_threads": os.cpu_count(),
                     "what": "parse + tokenize + System One layout of the rank's requests on all host threads"}
         line = base_line(args, METRIC + " (request stream)", total_real / (ms_max / 1e3), UNIT, d.world,
-                         ms_max / steps, cfg, padded_tokens_per_s=d.allsum(padded) / (ms_max / 1e3),
+                         ms_max / steps, cfg, padded_tokens_per_s=padded_all / (ms_max / 1e3),
                          device_makespan_s=ms_max / 1e3, e2e=e2e, frontend=frontend, gpu_launches=launches,
                          clocks=clk, cpu_baseline=cpu)
         line["steps"] = steps
