@@ -22,8 +22,14 @@
 // accumulates O.  No rescaling of O is needed.  Key blocks outside the band
 // are skipped.
 //
-// One CTA per (block, head), 4 warps, 82 KB shared memory and 256 TMEM
-// columns, so two CTAs share an SM.  Every wait is bounded.
+// Sequences of at most 128 tokens take the single-pass variant, with whole
+// consecutive sequences packed into one 128-row tile (they are adjacent in
+// the compacted rows): each query row's visible keys are the interval of its
+// own sequence (+-64 on local layers), so the packing changes no result and
+// the tiles carry fewer padding rows.  48 KB shared memory and 128 TMEM
+// columns (P aliases Q and K, O aliases S): four CTAs per SM.  Longer
+// sequences: one CTA per (128-row block, head), 82 KB shared memory and 256
+// TMEM columns, two CTAs per SM.  Every wait is bounded.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -144,9 +150,13 @@ __global__ void __launch_bounds__(THREADS, Layout<kSingle>::MIN_BLOCKS)
   grid_dep_trigger();
   const int tid = threadIdx.x, warp = tid >> 5;
   const int2 blk = a.blocks[blockIdx.x];
-  const int b = blk.x, q0 = blk.y, h = blockIdx.y;
-  const int len = a.seq_len[b];
-  const int row_base = a.seq_start[b];
+  const int h = blockIdx.y;
+  // kSingle: blk = (first row, rows) of a tile of whole sequences packed back
+  // to back; `len` is then the tile's row count and positions count from its
+  // first row.  Otherwise blk = (sequence, first query row).
+  const int b = kSingle ? 0 : blk.x, q0 = kSingle ? 0 : blk.y;
+  const int len = kSingle ? blk.y : a.seq_len[b];
+  const int row_base = kSingle ? blk.x : a.seq_start[b];
   const int window = a.window;
 
   int k_lo = 0, k_hi = len;
@@ -205,11 +215,23 @@ __global__ void __launch_bounds__(THREADS, Layout<kSingle>::MIN_BLOCKS)
   bool ok = true;
   float m_row = -INFINITY, l_row = 0.0f;
   RowRange rr{0, len};
-  if (window >= 0) {
-    rr.lo = r - window > 0 ? r - window : 0;
-    rr.hi = r + window + 1 < len ? r + window + 1 : len;
+  if (kSingle) {
+    // the keys of this row's own sequence (tile-relative), +-window on
+    // local layers
+    rr.lo = rr.hi = 0;
+    if (r < len) {
+      const int s = a.rowseq[row_base + r];
+      const int st = a.seq_start[s] - row_base, en = st + a.seq_len[s];
+      rr.lo = window >= 0 && r - window > st ? r - window : st;
+      rr.hi = window >= 0 && r + window + 1 < en ? r + window + 1 : en;
+    }
+  } else {
+    if (window >= 0) {
+      rr.lo = r - window > 0 ? r - window : 0;
+      rr.hi = r + window + 1 < len ? r + window + 1 : len;
+    }
+    if (r >= len) rr.hi = rr.lo;  // a row past the sequence: never stored, no scores
   }
-  if (r >= len) rr.hi = rr.lo;  // a row past the sequence: never stored, no scores
 
   // This row of S is streamed from TMEM one 32-key chunk at a time (a
   // second read is cheaper than holding 128 scores in registers).

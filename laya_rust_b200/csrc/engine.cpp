@@ -185,8 +185,8 @@ struct Weight {
 // Host-side plan of one request: validated and compacted (real tokens only).
 // Rows [row0, row0 + rows) of the compacted batch (whole sequences) whose
 // encoder and head layers run as one chain of launches; its attention blocks
-// are blocks[blk0, blk0 + nshort) (sequences of at most kAttnTcQRows tokens)
-// followed by nlong blocks of longer sequences.
+// are blocks[blk0, blk0 + nshort) (tiles of consecutive sequences of at most
+// kAttnTcQRows tokens) followed by nlong blocks of longer sequences.
 struct RowGroup {
   int row0 = 0, rows = 0, blk0 = 0, nshort = 0, nlong = 0;
 };
@@ -210,9 +210,10 @@ bool row_groups_enabled() {
 
 struct HostPlan {
   int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
-  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row;
-  // attention work: (sequence, first query row), kAttnTcQRows apart, grouped
-  // by row group
+  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row, rowseq;
+  // attention work per row group: tiles (first row, rows) packing whole
+  // consecutive sequences of at most kAttnTcQRows tokens, then (sequence,
+  // first query row) blocks of longer ones, kAttnTcQRows apart
   std::vector<int2> blocks;
   std::vector<RowGroup> groups;
   std::vector<uint8_t> rowtype;
@@ -221,7 +222,7 @@ struct HostPlan {
 
 // Offsets of each array inside one packed device buffer.
 struct PlanLayout {
-  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, blocks, rowtype, mmask, total;
+  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, blocks, rowtype, mmask, rowseq, total;
 };
 
 size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -243,6 +244,7 @@ PlanLayout layout_for(const HostPlan& p) {
   L.blocks = take(sizeof(int2) * p.nblocks);
   L.rowtype = take(p.R);
   L.mmask = take((size_t)p.n * p.k);
+  L.rowseq = take(sizeof(int) * p.R);
   L.total = o;
   return L;
 }
@@ -257,6 +259,30 @@ void pack(const HostPlan& p, const PlanLayout& L, uint8_t* dst) {
   memcpy(dst + L.blocks, p.blocks.data(), sizeof(int2) * p.nblocks);
   memcpy(dst + L.rowtype, p.rowtype.data(), p.R);
   memcpy(dst + L.mmask, p.mmask.data(), (size_t)p.n * p.k);
+  memcpy(dst + L.rowseq, p.rowseq.data(), sizeof(int) * p.R);
+}
+
+// Attention tiles for the sequences of at most kAttnTcQRows tokens among
+// [b0, b1): consecutive ones (adjacent in the compacted rows) share a tile
+// while their rows fit, as (first row, rows).
+void pack_short_tiles(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
+                      std::vector<int2>& out) {
+  int row0 = -1, rows = 0;
+  for (int b = b0; b < b1; ++b) {
+    if (len[b] > kAttnTcQRows) {
+      if (row0 >= 0) out.push_back(make_int2(row0, rows));
+      row0 = -1;
+      continue;
+    }
+    if (row0 >= 0 && start[b] == row0 + rows && rows + len[b] <= kAttnTcQRows) {
+      rows += len[b];
+    } else {
+      if (row0 >= 0) out.push_back(make_int2(row0, rows));
+      row0 = start[b];
+      rows = len[b];
+    }
+  }
+  if (row0 >= 0) out.push_back(make_int2(row0, rows));
 }
 
 // Validates a Req and compacts its real tokens.  The reference asserts
@@ -297,6 +323,7 @@ HostPlan make_plan(const laya_req* q) {
   p.tok.resize(R);
   p.pos.resize(R);
   p.rowtype.resize(R);
+  p.rowseq.resize(R);
   for (int b = 0; b < p.n; ++b) {
     const int64_t* ids = q->ids + (size_t)b * p.l;
     for (int t = 0; t < p.l; ++t)
@@ -306,6 +333,7 @@ HostPlan make_plan(const laya_req* q) {
       p.tok[p.seq_start[b] + t] = (int)ids[t];
       p.pos[p.seq_start[b] + t] = t;
       p.rowtype[p.seq_start[b] + t] = (uint8_t)q->qtype[b];
+      p.rowseq[p.seq_start[b] + t] = b;
     }
   }
   // two row groups of about R/2 rows, split at a sequence boundary
@@ -327,8 +355,7 @@ HostPlan make_plan(const laya_req* q) {
     g.row0 = p.seq_start[b0];
     g.rows = (b1 < p.n ? p.seq_start[b1] : R) - g.row0;
     g.blk0 = (int)p.blocks.size();
-    for (int b = b0; b < b1; ++b)
-      if (p.seq_len[b] <= kAttnTcQRows) p.blocks.push_back(make_int2(b, 0));
+    pack_short_tiles(p.seq_start, p.seq_len, b0, b1, p.blocks);
     g.nshort = (int)p.blocks.size() - g.blk0;
     for (int b = b0; b < b1; ++b)
       if (p.seq_len[b] > kAttnTcQRows)
@@ -662,7 +689,7 @@ struct Engine {
     const RowGroup& g = dp.host.groups[gi];
     const PlanLayout& L = dp.lay;
     AttnArgs aa{qkv.as<__half>(), ctx.as<__half>(), dp.at<int>(L.seq_start), dp.at<int>(L.seq_len),
-                dp.at<int2>(L.blocks) + g.blk0, window};
+                dp.at<int2>(L.blocks) + g.blk0, window, dp.at<int>(L.rowseq)};
     if (g.nshort > 0) {
       ck(launch_attention_tc(&dp.maps.qkv_tiles, aa, g.nshort, true, err.as<int>(), s), "attention");
       ++nl;
@@ -1459,26 +1486,30 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
       len[b] = lens[b];
       R += lens[b];
     }
-    // tcgen05: short sequences first (one block each), then the long ones
+    // tcgen05: tiles of consecutive short sequences first, then the long ones
     int nshort = 0;
-    if (impl == 1)
-      for (int b = 0; b < n; ++b)
-        if (len[b] <= qrows) blocks.push_back(make_int2(b, 0));
+    if (impl == 1) laya::pack_short_tiles(start, len, 0, n, blocks);
     nshort = (int)blocks.size();
+    std::vector<int> rowseq(R);
+    for (int b = 0; b < n; ++b)
+      for (int t = 0; t < len[b]; ++t) rowseq[start[b] + t] = b;
     for (int b = 0; b < n; ++b)
       if (impl == 0 || len[b] > qrows)
         for (int q0 = 0; q0 < len[b]; q0 += qrows) blocks.push_back(make_int2(b, q0));
-    laya::DevBuf dq, dout, ds, dl, db, derr;
+    laya::DevBuf dq, dout, ds, dl, db, drs, derr;
     dq.alloc((size_t)R * 3072 * 2, "qkv");
     dout.alloc((size_t)R * 1024 * 2, "out");
     ds.alloc(n * 4, "start");
     dl.alloc(n * 4, "len");
     db.alloc(blocks.size() * sizeof(int2), "blocks");
+    drs.alloc((size_t)R * 4, "rowseq");
+    laya::ck(cudaMemcpy(drs.p, rowseq.data(), (size_t)R * 4, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(dq.p, qkv, dq.bytes, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(ds.p, start.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(dl.p, len.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemcpy(db.p, blocks.data(), blocks.size() * sizeof(int2), cudaMemcpyHostToDevice), "h2d");
-    laya::AttnArgs a{dq.as<__half>(), dout.as<__half>(), ds.as<int>(), dl.as<int>(), db.as<int2>(), window};
+    laya::AttnArgs a{dq.as<__half>(), dout.as<__half>(), ds.as<int>(), dl.as<int>(), db.as<int2>(), window,
+                     drs.as<int>()};
     if (impl == 1) {
       derr.alloc(256, "err");
       laya::ck(cudaMemset(derr.p, 0, 256), "memset");

@@ -80,15 +80,21 @@ struct AttnArgs {
   __half* out;          // [R, 1024]
   const int* seq_start; // [n]
   const int* seq_len;   // [n]
-  const int2* blocks;   // [num_blocks] = (sequence, first query row within it)
+  // [num_blocks]: for sequences of at most kAttnTcQRows tokens (the tcgen05
+  // single-pass launch) (first row, rows) of a tile of whole consecutive
+  // sequences packed back to back; otherwise (sequence, first query row)
+  const int2* blocks;
   int window;           // < 0: global
+  const int* rowseq;    // [R] sequence of each row (packed tiles)
 };
 cudaError_t launch_attention(const AttnArgs& a, int num_blocks, cudaStream_t stream);
 constexpr int kAttnQRows = 64;
 // tcgen05 attention: blocks of kAttnTcQRows query rows; tm_qkv maps the qkv
 // buffer ([R, 3072] f16, box 64 columns x 128 rows, 128-byte swizzle).
-// short_seqs: every block's sequence has at most kAttnTcQRows tokens (one key
-// block, single pass, four CTAs per SM); otherwise the two-pass kernel.
+// short_seqs: the blocks are packed tiles of sequences of at most
+// kAttnTcQRows tokens (one key block, single pass, four CTAs per SM; each
+// query row sees only its own sequence's keys); otherwise the two-pass kernel
+// over (sequence, first query row) blocks.
 constexpr int kAttnTcQRows = 128;
 cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_blocks, bool short_seqs,
                                 int* err, cudaStream_t stream);
