@@ -290,3 +290,31 @@ def test_number_formatting_follows_ryu():
              0.1: "0.1", 1.2345678901234568e20: "1.2345678901234568e20", -0.0: "-0.0", 5e-324: "5e-324"}
     for x, s in cases.items():
         assert F.fmt_f64(x) == s
+
+
+def test_front_end_calls_reject_bad_arguments(tok):
+    """Null pointers and out-of-range indices come back as a status and a
+    message, never a crash (the engine ABI's convention)."""
+    import ctypes
+    L = FE.lib()
+    h = ctypes.c_void_p()
+    assert L.laya_tokenizer_from_json(None, 0, ctypes.byref(h)) != 0
+    assert L.laya_tokenizer_from_gguf(b"/nonexistent.gguf", ctypes.byref(h)) != 0
+    assert "nonexistent" in L.laya_last_error().decode()
+    n = ctypes.c_size_t()
+    assert L.laya_tokenize(None, b"x", 1, 0, None, 0, ctypes.byref(n)) != 0
+    rq = FE.Requests(tok, [GOLD["fixtures"][0]["request"]])
+    assert L.laya_requests_error(rq._h, 5) is not None          # out of range
+    with pytest.raises(FE.LayaError):
+        rq.question(10 ** 6)
+    with pytest.raises(FE.LayaError):
+        rq.batch(0)                                               # not packed yet
+    rq.pack(16384)
+    with pytest.raises(FE.LayaError):
+        rq.batch(99)
+    with pytest.raises(FE.LayaError, match="not scored"):
+        rq.response_text(0)
+    with pytest.raises(FE.LayaError):
+        rq.set_calibration((1.0, 1.0, 1.0), "[1, 2]")             # not an object
+    assert L.laya_requests_pack(rq._h, 0, 0, ctypes.byref(ctypes.c_int64())) != 0
+    rq.close()
