@@ -691,11 +691,12 @@ void plan_one(const Tokenizer& tok, const char* text, size_t len, Request& r, st
                                         " markers)");
       items.push_back(std::move(it));
     }
-  } catch (const json::ParseError& e) {
-    r.error = e.what();
+  } catch (const std::bad_alloc&) {
+    // runs on a worker thread: nothing may escape it
+    r.error = "out of host memory";
     items.clear();
-  } catch (const Error& e) {
-    r.error = e.what();
+  } catch (const std::exception& e) {
+    r.error = e.what();  // json::ParseError and Error carry the reference's messages
     items.clear();
   }
 }
