@@ -9,6 +9,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstring>
+#include <functional>
 #include <memory>
 #include <new>
 #include <stdexcept>
@@ -210,9 +211,17 @@ struct Tokenizer {
   std::vector<Added> added;  // longest content (in bytes) first, stable
   std::string byte_sym[256];  // UTF-8 of each byte's printable stand-in
   int64_t cls = 0, sep = 0, mask = 0, pad = 0, unk = 0;
+  // the merge table over interned symbols: (left, right) -> (rank, merged);
+  // symbol strings never contain ' ' (byte 0x20 stands as U+0120), so only
+  // merges "a b" with a single space can ever apply
+  std::unordered_map<std::string, int32_t> sym_id;
+  std::vector<int64_t> sym_vocab;  // vocabulary id of each interned symbol (or unk)
+  std::unordered_map<uint64_t, std::pair<int32_t, int32_t>> merge_tab;
+  int32_t byte_id[256];
 
   static std::unique_ptr<Tokenizer> from_json(const char* text, size_t len);
-  std::vector<std::string> bpe(std::vector<std::string> syms) const;
+  int32_t intern(const std::string& s);
+  std::vector<int32_t> bpe_ids(const std::string& bytes) const;
   void encode_chunk(const std::u32string& text, std::vector<int64_t>& out,
                     std::unordered_map<std::string, std::vector<int64_t>>* cache) const;
   std::vector<int64_t> encode(const std::u32string& text, bool add_special,
@@ -288,45 +297,97 @@ std::unique_ptr<Tokenizer> Tokenizer::from_json(const char* text, size_t len) {
     const uint32_t cp = keep ? static_cast<uint32_t>(b) : static_cast<uint32_t>(256 + n++);
     append_utf8(cp, t->byte_sym[b]);
   }
+  for (int b = 0; b < 256; ++b) t->byte_id[b] = t->intern(t->byte_sym[b]);
+  for (const auto& kv : t->ranks) {
+    const size_t sp = kv.first.find(' ');
+    if (sp == std::string::npos || kv.first.find(' ', sp + 1) != std::string::npos) continue;
+    const std::string a = kv.first.substr(0, sp), b = kv.first.substr(sp + 1);
+    if (a.empty() || b.empty()) continue;
+    const int32_t ia = t->intern(a), ib = t->intern(b), iab = t->intern(a + b);
+    t->merge_tab[(static_cast<uint64_t>(static_cast<uint32_t>(ia)) << 32) | static_cast<uint32_t>(ib)] = {
+        static_cast<int32_t>(kv.second), iab};
+  }
   return t;
 }
 
-// tokenizer.rs:172-207: merge the lowest-ranked adjacent pair (the first one
-// on ties) everywhere, left to right, until none applies.
-std::vector<std::string> Tokenizer::bpe(std::vector<std::string> syms) const {
-  if (syms.size() < 2) return syms;
-  std::string key;
-  for (;;) {
-    int64_t best_rank = -1;
-    size_t at = 0;
-    for (size_t i = 0; i + 1 < syms.size(); ++i) {
-      key.assign(syms[i]);
-      key.push_back(' ');
-      key.append(syms[i + 1]);
-      const auto it = ranks.find(key);
-      if (it != ranks.end() && (best_rank < 0 || it->second < best_rank)) {
-        best_rank = it->second;
-        at = i;
-      }
-    }
-    if (best_rank < 0) break;
-    const std::string a = syms[at], b = syms[at + 1];
-    std::vector<std::string> next;
-    next.reserve(syms.size());
-    size_t i = 0;
-    while (i < syms.size()) {
-      if (i + 1 < syms.size() && syms[i] == a && syms[i + 1] == b) {
-        next.push_back(a + b);
-        i += 2;
-      } else {
-        next.push_back(std::move(syms[i]));
-        i += 1;
-      }
-    }
-    syms.swap(next);
-    if (syms.size() == 1) break;
+int32_t Tokenizer::intern(const std::string& s) {
+  const auto it = sym_id.find(s);
+  if (it != sym_id.end()) return it->second;
+  const int32_t id = static_cast<int32_t>(sym_vocab.size());
+  sym_id.emplace(s, id);
+  const auto v = vocab.find(s);
+  sym_vocab.push_back(v == vocab.end() ? unk : v->second);
+  return id;
+}
+
+// BPE of one pre-tokenised piece (tokenizer.rs:172-207).  The reference
+// rescans every adjacent pair after each round: find the lowest-ranked pair,
+// merge all its occurrences left to right without overlap, repeat.  The same
+// rounds here in O(n log n): a min-heap of (rank, position) over adjacent
+// pairs; all entries of the lowest rank are taken together, merged in
+// position order, and only then are the pairs they form pushed.  Entries a
+// merge made stale are recognised by looking the pair up again (a rank names
+// exactly one pair).
+std::vector<int32_t> Tokenizer::bpe_ids(const std::string& bytes) const {
+  const int n = static_cast<int>(bytes.size());
+  std::vector<int32_t> sym(n);
+  std::vector<int> prev(n), next(n);
+  std::vector<char> alive(n, 1);
+  for (int i = 0; i < n; ++i) {
+    sym[i] = byte_id[static_cast<unsigned char>(bytes[i])];
+    prev[i] = i - 1;
+    next[i] = i + 1 < n ? i + 1 : -1;
   }
-  return syms;
+  auto rank_of = [&](int p, int32_t* merged) -> int32_t {
+    const int q = next[p];
+    if (q < 0) return -1;
+    const auto it = merge_tab.find((static_cast<uint64_t>(static_cast<uint32_t>(sym[p])) << 32) |
+                                   static_cast<uint32_t>(sym[q]));
+    if (it == merge_tab.end()) return -1;
+    if (merged) *merged = it->second.second;
+    return it->second.first;
+  };
+  using Entry = std::pair<int32_t, int>;  // (rank, position)
+  std::vector<Entry> heap;
+  auto push = [&](int p) {
+    const int32_t r = p >= 0 ? rank_of(p, nullptr) : -1;
+    if (r >= 0) {
+      heap.emplace_back(r, p);
+      std::push_heap(heap.begin(), heap.end(), std::greater<Entry>());
+    }
+  };
+  for (int i = 0; i + 1 < n; ++i) push(i);
+  std::vector<int> round, merged;
+  while (!heap.empty()) {
+    const int32_t r = heap.front().first;
+    round.clear();
+    while (!heap.empty() && heap.front().first == r) {
+      std::pop_heap(heap.begin(), heap.end(), std::greater<Entry>());
+      round.push_back(heap.back().second);
+      heap.pop_back();
+    }
+    std::sort(round.begin(), round.end());
+    merged.clear();
+    for (const int p : round) {
+      int32_t m = 0;
+      if (!alive[p] || rank_of(p, &m) != r) continue;  // stale, or overlapped by a merge of this round
+      const int q = next[p];
+      sym[p] = m;
+      alive[q] = 0;
+      next[p] = next[q];
+      if (next[q] >= 0) prev[next[q]] = p;
+      merged.push_back(p);
+    }
+    for (const int p : merged)
+      if (alive[p]) {
+        push(prev[p]);
+        push(p);
+      }
+  }
+  std::vector<int32_t> out;
+  for (int i = 0; i >= 0 && i < n; i = next[i])
+    if (alive[i]) out.push_back(sym[i]);
+  return out;
 }
 
 // tokenizer.rs:209-218
@@ -343,14 +404,8 @@ void Tokenizer::encode_chunk(const std::u32string& text, std::vector<int64_t>& o
         continue;
       }
     }
-    std::vector<std::string> syms;
-    syms.reserve(bytes.size());
-    for (const char c : bytes) syms.push_back(byte_sym[static_cast<unsigned char>(c)]);
     std::vector<int64_t> ids;
-    for (const std::string& s : bpe(std::move(syms))) {
-      const auto it = vocab.find(s);
-      ids.push_back(it == vocab.end() ? unk : it->second);
-    }
+    for (const int32_t s : bpe_ids(bytes)) ids.push_back(sym_vocab[s]);
     out.insert(out.end(), ids.begin(), ids.end());
     if (cache) cache->emplace(bytes, std::move(ids));
   }

@@ -318,3 +318,22 @@ def test_front_end_calls_reject_bad_arguments(tok):
         rq.set_calibration((1.0, 1.0, 1.0), "[1, 2]")             # not an object
     assert L.laya_requests_pack(rq._h, 0, 0, ctypes.byref(ctypes.c_int64())) != 0
     rq.close()
+
+
+def test_long_pieces_match_and_stay_fast(tok, otok):
+    """BPE on long single pieces (a letters-only run, a repeated pattern):
+    the same tokens as the reference's merge loop, and a 50 000-character
+    piece tokenizes in well under a second (the reference's loop is cubic
+    in a piece's length)."""
+    import time
+    rng = np.random.default_rng(5)
+    parts = ["the", "tion", "aaaa", "stand", "ing", "ou", "ea", "x"]
+    for trial in range(200):
+        w = "".join(parts[int(i)] for i in rng.integers(0, len(parts), int(rng.integers(1, 80))))
+        s = ("" if trial % 2 else " ") + w
+        assert tok.encode(s) == otok.encode(s, False), s
+    s = "a" * 300 + "b" * 150 + "ab" * 150
+    assert tok.encode(s) == otok.encode(s, False)
+    t0 = time.perf_counter()
+    ids = tok.encode("stand" * 10000)
+    assert time.perf_counter() - t0 < 1.0 and len(ids) > 0
