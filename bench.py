@@ -66,7 +66,7 @@ LAYERS = (("global", 0), ("local", 1))
 # Mean DRAM bytes (read + write) per GEMM launch from one ncu capture of layer
 # 1's four GEMMs in the 16384-token forward (cold L2); see
 # profiles/gemm_tc_layer1_forward16k.md.
-GEMM_TRAFFIC = 64.7e6
+GEMM_TRAFFIC = 58.9e6
 
 
 def parse():
