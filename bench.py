@@ -63,9 +63,8 @@ CONFIGS = ["forward-16k", "long-state", "layer", "request", "stream"]
 DATA = "synthetic (seeded ids, random-init weights)"
 MODEL = "laya (ModernBERT-large 28L + 2L head), random-init f16 GGUF seed 0"
 LAYERS = (("global", 0), ("local", 1))
-# Mean DRAM bytes (read + write) per GEMM launch from one ncu capture of layer
-# 1's four GEMMs in the 16384-token forward (cold L2); see
-# profiles/gemm_tc_layer1_forward16k.md.
+# Mean DRAM bytes (read + write) per GEMM launch from one ncu capture
+# (--set full) of layer 1's four GEMMs in the 16384-token forward (cold L2).
 GEMM_TRAFFIC = 58.9e6
 
 
@@ -488,7 +487,7 @@ def run_forward(args, d, eng):
                                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                                    "peak_source": f"{pk_src} bf16_tflops_sustained", "traffic": GEMM_TRAFFIC if args.config == "forward-16k" else None,
                                    "traffic_source": "ncu, layer 1's four GEMMs of the 16384-token forward, "
-                                                     "cold L2 (profiles/gemm_tc_layer1_forward16k.md)",
+                                                     "cold L2 (ncu --set full, gemm_tc_kernel, -s 4 -c 4)",
                                    "launches_per_step": gemm_launches // args.steps,
                                    "flops_per_step": workloads.gemm_flops(req)},
                          kernels=kernels, e2e=e2e, gpu_launches=launches * args.steps, clocks=clk,

@@ -6,7 +6,7 @@
  *   trait Engine { fn info(&self) -> EngineInfo; fn forward(&mut self, &Req) -> Out; }
  * (src/engine.rs:79-82) with Req (src/engine.rs:1-10) and Out
  * (src/engine.rs:12-17).  A Rust `CudaEngine` shim replacing
- * src/backend/cuda/mod.rs binds the functions below; INTEGRATION.md shows it.
+ * src/backend/cuda/mod.rs binds the functions below.
  *
  * Conventions
  *   - Every function returns LAYA_OK (0) or a nonzero status; the message of

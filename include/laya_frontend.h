@@ -93,7 +93,9 @@ int laya_requests_set_calibration(laya_requests *r, const float *temperature, co
 int laya_requests_score(laya_requests *r, int64_t f, const float *logits, const float *act);
 /* The response of one request (main.rs:551-557) as compact JSON:
  * {"model":"laya","answers":{...},"usage":{"input_tokens":T,"output_tokens":0}}
- * with answers in the order they were scored.  *len receives the full
+ * with answers in the order run_all scores the request alone (sequence
+ * length, ties in question order: group_by_budget's stable sort,
+ * main.rs:448-450), however its questions were packed.  *len receives the full
  * length; at most cap bytes are written (no terminator is added).  Fails if
  * a question of the request is not scored yet. */
 int laya_requests_response(const laya_requests *r, int64_t request, char *buf, size_t cap, size_t *len);

@@ -19,7 +19,7 @@ LIB = os.path.join(LIB_DIR, "liblaya_b200.so")
 OBJ_DIR = os.path.join(ROOT, "_build", "obj")
 
 SOURCES = ["gemm.cu", "attention.cu", "attn_tc.cu", "rownorm.cu", "tail.cu", "tail_static.cu", "engine.cpp",
-           "gguf_reader.cpp", "json.cpp", "frontend.cpp"]
+           "gguf_reader.cpp", "json.cpp", "frontend.cpp", "serve.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "gguf_reader.h", "json.h", "unicode_tables.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -38,7 +38,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     os.makedirs(LIB_DIR, exist_ok=True)
     os.makedirs(OBJ_DIR, exist_ok=True)
     hdrs = [os.path.join(CSRC, h) for h in HEADERS] + [os.path.join(ROOT, "include", h)
-                                                       for h in ("laya_b200.h", "laya_frontend.h")]
+                                                       for h in ("laya_b200.h", "laya_frontend.h", "laya_serve.h")]
     objs = []
     for src in SOURCES:
         s = os.path.join(CSRC, src)

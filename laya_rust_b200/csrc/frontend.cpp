@@ -708,7 +708,6 @@ struct Item {
   int64_t qtype = 0;
   // scoring
   bool scored = false;
-  int64_t order = 0;  // (forward, row) in scoring order
   json::Value ans;
 };
 
@@ -1029,7 +1028,6 @@ int laya_requests_score(laya_requests* r, int64_t f, const float* logits, const 
       const auto& q = R.reqs[it.request].questions[it.q];
       it.ans = laya::fe::answer(q, probs, act_p);
       it.scored = true;
-      it.order = (f << 20) + row;
     }
   });
 }
@@ -1047,7 +1045,10 @@ int laya_requests_response(const laya_requests* r, int64_t request, char* buf, s
       if (!R.items[i].scored) throw Error(LAYA_E_STATE, "a question of this request is not scored yet");
       tokens += static_cast<int64_t>(R.items[i].seq.size());
     }
-    std::stable_sort(order.begin(), order.end(), [&](int64_t a, int64_t b) { return R.items[a].order < R.items[b].order; });
+    // the order run_all scores them for this request alone: group_by_budget's
+    // stable sort by sequence length (main.rs:448-450), whatever the packing
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int64_t a, int64_t b) { return R.items[a].seq.size() < R.items[b].seq.size(); });
     laya::json::Value answers = laya::json::Value::object();
     for (const int64_t i : order) answers.set(rq.questions[R.items[i].q].id, R.items[i].ans);
     laya::json::Value usage = laya::json::Value::object();

@@ -1,5 +1,5 @@
 """The C-ABI library: it loads, exports every function include/laya_b200.h
-declares, and fails with a status code (never an abort) when there is no GPU
+declares (engine, front end, HTTP service), and fails with a status code (never an abort) when there is no GPU
 or the arguments are bad.  No compute runs here."""
 import ctypes
 import os
@@ -10,7 +10,7 @@ import pytest
 from laya_rust_b200 import engine as E
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-HEADERS = [os.path.join(ROOT, "include", h) for h in ("laya_b200.h", "laya_frontend.h")]
+HEADERS = [os.path.join(ROOT, "include", h) for h in ("laya_b200.h", "laya_frontend.h", "laya_serve.h")]
 
 
 def declared_functions():

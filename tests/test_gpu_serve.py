@@ -1,0 +1,101 @@
+"""The HTTP service on a B200 with a real engine: 200 bodies byte-identical
+to the library's own request path (run_requests through laya_forward on a
+second engine), the 422 contract through the engine-backed service, and
+cross-request batching under concurrent clients (same questions, same
+choices, probabilities within 2e-3 of the one-request-at-a-time answers:
+batching moves rows between attention tiles, which may change the last bits
+of a softmax sum)."""
+import http.client
+import json
+import threading
+
+import numpy as np
+import pytest
+
+from laya_rust_b200 import engine as E
+from laya_rust_b200 import frontend as FE
+from laya_rust_b200 import modelgen, tokgen, workloads
+from laya_rust_b200 import serve as S
+
+pytestmark = pytest.mark.gpu
+
+
+def bodies(n, seed):
+    words = workloads.vocab_words(tokgen.tokenizer_json(0))
+    rng = np.random.default_rng(seed)
+    out = [workloads.single_request_json(words, 0)]
+    out += [workloads.system_one_request_json(rng, words, int(rng.integers(20, 400)),
+                                              workloads.random_questions(rng)[:int(rng.integers(1, 8))])
+            for _ in range(n - 1)]
+    return [json.dumps(b) for b in out]
+
+
+def post(addr, body):
+    host, port = addr.split(":")
+    c = http.client.HTTPConnection(host, int(port), timeout=120)
+    c.request("POST", "/systemone", body=body)
+    r = c.getresponse()
+    d = r.read()
+    c.close()
+    return r.status, d
+
+
+@pytest.fixture(scope="module")
+def direct():
+    path = modelgen.cached_model(seed=0)
+    eng = E.Engine(path, device=0)
+    tok = FE.Tokenizer(gguf_path=path)
+    info = eng.info()
+    yield path, eng, tok, info.calibration
+    tok.close()
+    eng.close()
+
+
+def test_served_bodies_equal_the_library_request_path(direct):
+    path, eng, tok, cal = direct
+    bs = bodies(6, 3)
+    want = []
+    for b in bs:
+        rq = FE.Requests(tok, [b])
+        rq.set_calibration(cal["temperature"], cal["by_options"])
+        for f in range(rq.pack(16384)):
+            out = eng.forward(rq.batch(f))
+            rq.score(f, out.logits, out.act)
+        want.append(rq.response_text(0))
+        rq.close()
+    with S.Server(model=path, addr="127.0.0.1:0", devices=(0,)) as s:
+        for b, w in zip(bs, want):
+            st, d = post(s.address, b)
+            assert st == 200 and d.decode() == w
+        st, d = post(s.address, '{"state": "x", "questions": {}}')
+        assert (st, json.loads(d)) == (422, {"error": "no questions"})
+
+
+def test_batched_service_under_concurrent_clients(direct):
+    path, eng, tok, cal = direct
+    bs = bodies(24, 7)
+    with S.Server(model=path, addr="127.0.0.1:0", devices=(0,)) as s:
+        one = [post(s.address, b) for b in bs]
+    res = [None] * len(bs)
+    with S.Server(model=path, addr="127.0.0.1:0", devices=(0,), batch=16, connections=24) as s:
+        ts = [threading.Thread(target=lambda i=i: res.__setitem__(i, post(s.address, bs[i])))
+              for i in range(len(bs))]
+        for t in ts:
+            t.start()
+        for t in ts:
+            t.join(300)
+        st = s.stats()
+    assert st["200"] == len(bs) and st["forwards"] <= len(bs)
+    for (s1, d1), (s2, d2) in zip(one, res):
+        assert s1 == 200 and s2 == 200
+        a, b = json.loads(d1), json.loads(d2)
+        assert list(a["answers"]) == list(b["answers"]) and a["usage"] == b["usage"]
+        for qid, x in a["answers"].items():
+            y = b["answers"][qid]
+            assert x["type"] == y["type"]
+            if x["type"] == "choice":
+                assert x["choice"] == y["choice"] and list(x["probabilities"]) == list(y["probabilities"])
+                for k, p in x["probabilities"].items():
+                    assert abs(p - y["probabilities"][k]) <= 2e-3
+            else:
+                assert abs(x["noul"] - y["noul"]) <= 2e-3
