@@ -208,6 +208,23 @@ bool row_groups_enabled() {
   return on;
 }
 
+// Split-K for the residual GEMMs (Wo, Wo_mlp) of small batches: when the
+// 256 x 256 output tiles fill at most half the clusters, the K loop is cut
+// into parts that run on otherwise idle SMs; each part stores its f32 sums
+// (kEpiPartial) and the LayerNorm that follows adds them to the residual in
+// part order, so results stay bitwise reproducible.  LAYA_SPLITK=0 turns it
+// off.  kPartRows bounds parts x padded rows over every M the rule admits
+// (at most 4608: e.g. 9 row blocks x 2 parts, 3 x 6).
+constexpr int kPartRows = 4608;
+
+bool splitk_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LAYA_SPLITK");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 struct HostPlan {
   int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
   std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row, rowseq;
@@ -442,6 +459,12 @@ struct Engine {
   int cap_rows = 0, cap_mk = 0, cap_n = 0;
   uint64_t arena_gen = 0;  // bumped on every reallocation; captured graphs record it
   DevBuf x, t16, qkv, ctx, gate, hmlp, mk16, partial, out_logits, out_act, err, plan_buf;
+  // split-K parts of the residual GEMMs, one region per row group, and the
+  // parts each group's next LayerNorm still has to add
+  DevBuf parts[2];
+  CUtensorMap parts_map[2];
+  bool parts_ready = false;
+  PendingParts pend[2];
   uint8_t* staging = nullptr;    // pinned host staging for plan uploads
   size_t staging_bytes = 0;
   float* pinned_out = nullptr;   // pinned staging for outputs
@@ -615,6 +638,7 @@ struct Engine {
   // ---- arena ----------------------------------------------------------------------
   void ensure_arena(const HostPlan& p) {
     ensure_rope(p.l);
+    ensure_parts();
     const int rows = (p.R + kGemmBM - 1) / kGemmBM * kGemmBM;
     const int mk = (p.n * p.k + kGemmBM - 1) / kGemmBM * kGemmBM;
     if (rows <= cap_rows && mk <= cap_mk && p.n <= cap_n) return;
@@ -636,6 +660,31 @@ struct Engine {
     out_act.alloc((size_t)cap_n * 2 * 4, "arena act");
     for (DevBuf* b : {&x, &t16, &qkv, &ctx, &gate, &hmlp, &mk16, &partial})
       ck(cudaMemset(b->p, 0, b->bytes), "arena clear");
+  }
+
+  // The split-K part regions: allocated once, with a plan (never while a
+  // stream is being captured).
+  void ensure_parts() {
+    if (parts_ready || !splitk_enabled()) return;
+    for (int g = 0; g < 2; ++g) {
+      parts[g].alloc((size_t)kPartRows * H * 4, "split-K parts");
+      if (make_tmap_2d(&parts_map[g], parts[g].p, true, kPartRows, H, 32, kGemmOutBoxRows))
+        throw Error(LAYA_E_CUDA, "tensor map encode failed for the split-K parts");
+    }
+    parts_ready = true;
+  }
+
+  // K parts for a residual GEMM of M rows: 1 (no split) unless its tiles
+  // fill at most half the clusters; then as many as fill the clusters, at
+  // least 4 k-blocks each, at most 8, within the part region.
+  int choose_splits(int M, int K) const {
+    if (!parts_ready) return 1;
+    const int num_m = (M + kGemmBM - 1) / kGemmBM, tiles = num_m * (H / kGemmBN);
+    const int clusters = num_sms / 2;
+    if (tiles == 0 || tiles * 2 > clusters) return 1;
+    int S = std::min(std::min(clusters / tiles, (K / kGemmBK) / 4), 8);
+    while (S > 1 && S * num_m * kGemmBM > kPartRows) --S;
+    return S;
   }
 
   void ensure_maps(DevicePlan& dp) {
@@ -703,16 +752,45 @@ struct Engine {
     }
   }
 
-  void row_ln(const float* xin, const std::string& wname, const float* b, __half* out, int rows, cudaStream_t s,
+  // LayerNorm of row group gi's residual rows into `out`; first adds the
+  // split-K parts the group's last residual GEMM left, if any.
+  void row_ln(int gi, float* xin, const std::string& wname, const float* b, __half* out, int rows, cudaStream_t s,
               int64_t& nl) {
-    ck(launch_ln(xin, nullptr, W(wname).buf.as<float>(), b, EPS, out, rows, s), "ln");
+    if (pend[gi].nparts > 0) {
+      ck(launch_ln_parts(xin, pend[gi], W(wname).buf.as<float>(), b, EPS, out, rows, s), "ln parts");
+      pend[gi] = PendingParts();
+    } else {
+      ck(launch_ln(xin, nullptr, W(wname).buf.as<float>(), b, EPS, out, rows, s), "ln");
+    }
     ++nl;
     mark(kProfNorm);
+  }
+
+  // x += A . W^T for an encoder residual GEMM (no bias).  With `defer`
+  // (a LayerNorm of the same rows comes next) and a small M, the K loop is
+  // split and the sums stay pending for that LayerNorm.
+  void resid_gemm(int gi, const CUtensorMap& A, const Weight& Wt, const CUtensorMap& Out, int R, int K, cudaStream_t s,
+                  int64_t& nl, int kind, bool defer) {
+    GemmArgs r{};
+    r.ldo = H;
+    const int S = defer ? choose_splits(R, K) : 1;
+    if (S < 2) {
+      gemm(kEpiResid, A, Wt, Out, R, H, K, r, s, nl, kind);
+      return;
+    }
+    if (pend[gi].nparts > 0) throw Error(LAYA_E_STATE, "split-K parts of an earlier GEMM were not consumed");
+    r.splits = S;
+    r.split_rows = (R + kGemmBM - 1) / kGemmBM * kGemmBM;
+    gemm(kEpiPartial, A, Wt, parts_map[gi], R, H, K, r, s, nl, kind);
+    pend[gi] = PendingParts{parts[gi].as<float>(), S, (size_t)r.split_rows * H};
   }
 
   // Encoder layer `layer` (graph.rs:104-123) for row group gi on stream s.
   // In the forward (`embedded`), layer 0's input norm is the embedding norm,
   // already applied by embed_ln.
+  // Wo_mlp's split-K parts, if any, stay pending for the LayerNorm after
+  // this layer (the next layer's input norm, or the final norm); a caller
+  // that reads the residual stream first folds them in (fold_parts).
   void enc_layer(const DevicePlan& dp, int gi, int layer, cudaStream_t s, int64_t& nl, bool embedded = true) {
     const RowGroup& g = dp.host.groups[gi];
     const GroupMaps& M = dp.maps.g[gi];
@@ -722,7 +800,7 @@ struct Engine {
     float* xg = x.as<float>() + r0 * H;
     __half* tg = t16.as<__half>() + r0 * H;
     if (layer > 0) {
-      row_ln(xg, attn_norm(layer), nullptr, tg, R, s, nl);
+      row_ln(gi, xg, attn_norm(layer), nullptr, tg, R, s, nl);
     } else if (!embedded) {
       // layer 0 alone: its input norm is the embedding norm, and its residual
       // base is the normed input (graph.rs:112-113), so x itself is normed
@@ -739,17 +817,25 @@ struct Engine {
     gemm(kEpiQkvRope, M.a_t16, W(fmt("encoder.layers.%d.attn.Wqkv.weight", layer)), M.o_qkv, R, 3 * H, H, q, s, nl,
          kProfQkv);
     attention(dp, gi, global ? -1 : WINDOW, s, nl);
-    GemmArgs r{};
-    r.ldo = H;
-    gemm(kEpiResid, M.a_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), M.o_x, R, H, H, r, s, nl, kProfWo);
-    row_ln(xg, fmt("encoder.layers.%d.mlp_norm.weight", layer), nullptr, tg, R, s, nl);
+    resid_gemm(gi, M.a_ctx, W(fmt("encoder.layers.%d.attn.Wo.weight", layer)), M.o_x, R, H, s, nl, kProfWo, true);
+    row_ln(gi, xg, fmt("encoder.layers.%d.mlp_norm.weight", layer), nullptr, tg, R, s, nl);
     GemmArgs gg{};
     gg.ldo = INTER;
     gg.n_valid = INTER;
     gemm(kEpiGeglu, M.a_t16, W(fmt("encoder.layers.%d.mlp.Wi.weight", layer)), M.o_gate, R, 2 * INTER_PAD, H, gg, s,
          nl, kProfWi);
-    gemm(kEpiResid, M.a_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), M.o_x, R, H, INTER, r, s, nl,
-         kProfWo2);
+    resid_gemm(gi, M.a_gate, W(fmt("encoder.layers.%d.mlp.Wo.weight", layer)), M.o_x, R, INTER, s, nl, kProfWo2,
+               true);
+  }
+
+  // Adds row group gi's pending split-K parts to its residual rows.
+  void fold_parts(const DevicePlan& dp, int gi, cudaStream_t s, int64_t& nl) {
+    if (pend[gi].nparts == 0) return;
+    const RowGroup& g = dp.host.groups[gi];
+    ck(launch_add_parts(x.as<float>() + (size_t)g.row0 * H, pend[gi], g.rows, s), "add parts");
+    pend[gi] = PendingParts();
+    ++nl;
+    mark(kProfNorm);
   }
 
   static std::string hn(int i, const char* s) { return fmt("head.layers.%d.%s", i, s); }
@@ -762,8 +848,9 @@ struct Engine {
     ck(launch_final_ln(x.as<float>() + r0 * H, W("encoder.final_norm.weight").buf.as<float>(),
                        W("type_emb.weight").buf.as<__half>(), dp.at<uint8_t>(dp.lay.rowtype) + r0,
                        W(hn(0, "norm1.weight")).buf.as<float>(), W(hn(0, "norm1.bias")).buf.as<float>(), EPS,
-                       t16.as<__half>() + r0 * H, g.rows, s),
+                       t16.as<__half>() + r0 * H, g.rows, s, pend[gi]),
        "final_ln");
+    pend[gi] = PendingParts();
     ++nl;
     mark(kProfNorm);
   }
@@ -777,7 +864,7 @@ struct Engine {
     const int R = g.rows;
     float* xg = x.as<float>() + r0 * H;
     __half* tg = t16.as<__half>() + r0 * H;
-    if (hl > 0) row_ln(xg, hn(hl, "norm1.weight"), W(hn(hl, "norm1.bias")).buf.as<float>(), tg, R, s, nl);
+    if (hl > 0) row_ln(gi, xg, hn(hl, "norm1.weight"), W(hn(hl, "norm1.bias")).buf.as<float>(), tg, R, s, nl);
     GemmArgs q{};
     q.ldo = 3 * H;
     q.bias = W(hn(hl, "self_attn.in_proj_bias")).buf.as<float>();
@@ -788,7 +875,7 @@ struct Engine {
     r.ldo = H;
     r.bias = W(hn(hl, "self_attn.out_proj.bias")).buf.as<float>();
     gemm(kEpiResid, M.a_ctx, W(hn(hl, "self_attn.out_proj.weight")), M.o_x, R, H, H, r, s, nl, kProfHead);
-    row_ln(xg, hn(hl, "norm2.weight"), W(hn(hl, "norm2.bias")).buf.as<float>(), tg, R, s, nl);
+    row_ln(gi, xg, hn(hl, "norm2.weight"), W(hn(hl, "norm2.bias")).buf.as<float>(), tg, R, s, nl);
     GemmArgs f{};
     f.ldo = HEAD_INTER;
     f.bias = W(hn(hl, "linear1.bias")).buf.as<float>();
@@ -872,9 +959,14 @@ struct Engine {
       ++nl;
       mark(kProfNorm);
     }
+    pend[0] = pend[1] = PendingParts();
     for (int layer = 0; layer < NLAYER; ++layer) {
       for (int gi = 0; gi < G; ++gi) enc_layer(dp, gi, layer, group_stream(gi, conc), nl);
-      if (tap) emit_rows(dp, fmt("enc.%d", layer).c_str(), tap, user);
+      if (tap) {
+        // taps read the residual stream after each layer
+        for (int gi = 0; gi < G; ++gi) fold_parts(dp, gi, group_stream(gi, conc), nl);
+        emit_rows(dp, fmt("enc.%d", layer).c_str(), tap, user);
+      }
     }
     for (int gi = 0; gi < G; ++gi) final_norm(dp, gi, group_stream(gi, conc), nl);
     if (tap) emit_rows(dp, "final", tap, user);
@@ -884,6 +976,7 @@ struct Engine {
     }
     join(conc);
     scorer_tail(dp, stream, nl);
+    if (pend[0].nparts || pend[1].nparts) throw Error(LAYA_E_STATE, "split-K parts left pending after the forward");
     return nl;
   }
 
@@ -896,7 +989,11 @@ struct Engine {
     const bool conc = G > 1 && !prof_ev;
     int64_t nl = 0;
     fork(conc);
-    for (int gi = 0; gi < G; ++gi) enc_layer(dp, gi, layer, group_stream(gi, conc), nl, false);
+    pend[0] = pend[1] = PendingParts();
+    for (int gi = 0; gi < G; ++gi) {
+      enc_layer(dp, gi, layer, group_stream(gi, conc), nl, false);
+      fold_parts(dp, gi, group_stream(gi, conc), nl);
+    }
     join(conc);
     return nl;
   }

@@ -23,6 +23,9 @@
 //               half of the tile): tcgen05.ld of 32 lanes, fused math, a
 //               128-byte-swizzled shared staging tile, then a TMA store
 //               (or TMA reduce-add for the f32 residual) of 32 rows at a time
+// With kEpiPartial (small M), a work unit is a (tile, K part) pair: the
+// clusters split each tile's K loop and store f32 part sums, which the next
+// row kernel adds in part order.
 // No TMA load in this kernel uses multicast; every CTA loads its own operand
 // halves.  The MMA completion signal is delivered to both CTAs of the pair
 // with tcgen05.commit's cluster-multicast form.
@@ -228,7 +231,7 @@ struct Stager {
 // [hc*BN/4, (hc+1)*BN/4), from gate and up columns of that range).
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmOut, Stager& st,
-                                              uint32_t t_row, int row0, int row, int n0, int hc) {
+                                              uint32_t t_row, int row0, int row, int n0, int hc, int yoff) {
   const bool valid = row < a.M;
   const int r = row - row0;  // row within this warp's 32-row slab
   const int cb = hc * (BN / 2), ce = cb + BN / 2;
@@ -307,7 +310,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       stage_row(s, r, w);
       st.store(tmOut, n0 + c0, row0, false);
     }
-  } else if constexpr (EPI == kEpiResid || EPI == kEpiStoreF32) {
+  } else if constexpr (EPI == kEpiResid || EPI == kEpiStoreF32 || EPI == kEpiPartial) {
 #pragma unroll 1
     for (int c0 = cb; c0 < ce; c0 += 32) {
       uint32_t v[32];
@@ -320,7 +323,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       }
       uint8_t* s = st.acquire();
       stage_row(s, r, v);
-      st.store(tmOut, n0 + c0, row0, EPI == kEpiResid);
+      // a part's rows start at yoff (kEpiPartial); 0 otherwise
+      st.store(tmOut, n0 + c0, row0 + yoff, EPI == kEpiResid);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     const int oc0 = (n0 / BN) * (BN / 2);
@@ -389,6 +393,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_n = args.N / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = args.K / BK;
+  // work unit u = (tile u / S, K part u % S): part p covers k-blocks
+  // [p * num_kb / S, (p + 1) * num_kb / S).  S = 1 except for kEpiPartial.
+  const int S = EPI == kEpiPartial ? args.splits : 1;
+  const int num_units = num_tiles * S;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -429,10 +437,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       // the A operand is read by the num_n clusters working on its row block
       // at about the same time, and not after: evict-first
       const uint64_t pol_a = l2_evict_first();
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int tile = u / S, part = u - tile * S;
         const int m0 = (tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
         const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int kb1 = (part + 1) * num_kb / S;
+        for (int kb = part * num_kb / S; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag)) {
             ok = false;
             break;
@@ -461,14 +471,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       int acc = 0;
       uint32_t aphase = 0;
       bool ok = true;
-      for (int tile = cluster_id; tile < num_tiles && ok; tile += num_clusters) {
+      for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
+        const int part = u % S;
+        const int kb0 = part * num_kb / S, kb1 = (part + 1) * num_kb / S;
         if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, args.err, kErrGemmMmaWait, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) {
             ok = false;
             break;
@@ -479,7 +491,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma2_f16(d_tmem, umma_desc_sw128(a_addr + k * 32), umma_desc_sw128(b_addr + k * 32), idesc,
-                      (kb | k) != 0 ? 1u : 0u);
+                      (kb != kb0 || k != 0) ? 1u : 0u);
           umma2_commit_both(&empty[stage]);
           if (++stage == C::STAGES) {
             stage = 0;
@@ -503,7 +515,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tempty_leader[2] = {map_to_rank(smem_u32(&tempty[0]), 0), map_to_rank(smem_u32(&tempty[1]), 0)};
     int acc = 0;
     uint32_t aphase = 0;
-    for (int tile = cluster_id; tile < num_tiles; tile += num_clusters) {
+    for (int u = cluster_id; u < num_units; u += num_clusters) {
+      const int tile = u / S, part = u - tile * S;
       int ok = 1;
       if (lane == 0)
         ok = mbar_wait_bounded(&tfull[acc], aphase, args.err, kErrGemmEpilogueWait, abort_flag);
@@ -515,7 +528,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row0 = m0 + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       st.active = row0 < args.M;
-      epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc);
+      epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc,
+                             EPI == kEpiPartial ? part * args.split_rows : 0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
@@ -549,8 +563,9 @@ cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cud
   }
   const int num_tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
   if (num_tiles == 0) return cudaSuccess;
+  const int num_units = num_tiles * (EPI == kEpiPartial ? args.splits : 1);
   const int max_clusters = num_sms / 2;
-  const int clusters = num_tiles < max_clusters ? num_tiles : max_clusters;
+  const int clusters = num_units < max_clusters ? num_units : max_clusters;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
@@ -566,6 +581,10 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
                         int bn) {
   if (bn != kGemmBN && bn != kGemmBNNarrow) return cudaErrorInvalidValue;
   if (args.N % bn || args.K % BK || args.M < 0 || !m.a || !m.b || !m.out) return cudaErrorInvalidValue;
+  if (epilogue == kEpiPartial &&
+      (bn != kGemmBN || args.splits < 1 || args.splits > args.K / BK || args.split_rows % BM ||
+       args.split_rows < ((args.M + BM - 1) / BM) * BM))
+    return cudaErrorInvalidValue;
   if (bn == kGemmBNNarrow) {
     // narrow tiles: the residual GEMMs with N = 1024 (more tiles per wave)
     if (epilogue == kEpiResid) return launch_one<kEpiResid, kGemmBNNarrow>(m, args, num_sms, stream);
@@ -580,6 +599,7 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
     case kEpiBiasRelu: return launch_one<kEpiBiasRelu, kGemmBN>(m, args, num_sms, stream);
     case kEpiScorer: return launch_one<kEpiScorer, kGemmBN>(m, args, num_sms, stream);
     case kEpiStoreF32: return launch_one<kEpiStoreF32, kGemmBN>(m, args, num_sms, stream);
+    case kEpiPartial: return launch_one<kEpiPartial, kGemmBN>(m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
 }

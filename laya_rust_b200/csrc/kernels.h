@@ -33,6 +33,11 @@ enum GemmEpilogue : int {
   kEpiBiasRelu = 4, // f16 out [M, N] = relu(acc + bias)
   kEpiScorer = 5,   // f32 partial[N/256][ldo] = sum_c gelu(acc + bias) * wvec
   kEpiStoreF32 = 6, // f32 out [M, N] = acc (tests)
+  // split-K partial sums: the K range is cut into `splits` parts and part s of
+  // tile (m, n) stores its f32 sum at output rows s * split_rows + m.  A row
+  // kernel adds the parts to the residual in part order (deterministic), so
+  // small-M GEMMs spread their K loop over more SMs.
+  kEpiPartial = 7,
 };
 
 struct GemmArgs {
@@ -49,6 +54,8 @@ struct GemmArgs {
   float scale;         // q/k scale
   const float* wvec;   // scorer output weights [N]
   int n_valid;         // valid output columns for kEpiGeglu
+  int splits;          // kEpiPartial: K parts (>= 1)
+  int split_rows;      // kEpiPartial: output rows per part (multiple of 256, >= M)
 };
 
 // Encodes a 2-D f16 K-major tensor map: rows x k elements, row stride k*2 B,
@@ -108,10 +115,25 @@ cudaError_t launch_ln(const float* x, const int* idx, const float* w, const floa
                       __half* t16, int rows, cudaStream_t s);
 // x[r] = t16[r] = LN(x[r]) * w  (each warp reads its row before writing it)
 cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, int rows, cudaStream_t s);
-// x[r] = LN(x[r]) * wf + type[rowtype[r]];  t16[r] = LN(x[r]) * w1 + b1
+// Split-K partial sums waiting to be added to the residual stream: part s of
+// row r is parts[s * stride + r * 1024 + c], s < nparts.
+struct PendingParts {
+  const float* parts = nullptr;
+  int nparts = 0;
+  size_t stride = 0;
+};
+// x[r] += sum_s parts[s][r] (parts summed in order, then added);
+// t16[r] = LN(x[r]) * w (+ b)
+cudaError_t launch_ln_parts(float* x, const PendingParts& p, const float* w, const float* b, float eps,
+                            __half* t16, int rows, cudaStream_t s);
+// x[r] += sum_s parts[s][r] (the same arithmetic as launch_ln_parts)
+cudaError_t launch_add_parts(float* x, const PendingParts& p, int rows, cudaStream_t s);
+// x[r] = LN(x[r] (+ pending parts)) * wf + type[rowtype[r]];
+// t16[r] = LN(x[r]) * w1 + b1
 cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb,
                             const uint8_t* rowtype, const float* w1, const float* b1,
-                            float eps, __half* t16, int rows, cudaStream_t s);
+                            float eps, __half* t16, int rows, cudaStream_t s,
+                            const PendingParts& pend = PendingParts());
 
 // ---- tail: scorer sum, post, act head --------------------------------------------
 struct TailArgs {

@@ -1,5 +1,6 @@
-// Row kernels: embedding gather + LayerNorm, LayerNorm (optionally gathered),
-// and the final norm + type embedding + first head norm.  One warp per
+// Row kernels: embedding gather + LayerNorm, LayerNorm (optionally gathered,
+// or after adding a split-K GEMM's parts to the residual), and the final
+// norm + type embedding + first head norm.  One warp per
 // 1024-wide row, the row held in registers (32 values per lane), two-pass f32
 // statistics, 512-byte coalesced loads and stores.
 //
@@ -102,6 +103,31 @@ __device__ __forceinline__ void scale_shift(float (&v)[32], int lane, const floa
   }
 }
 
+// v += sum of the split-K parts of this row, the parts summed in part order
+// first (so the result does not depend on which CTA finished first).  The
+// parts are read once: streaming loads.
+__device__ __forceinline__ void add_parts(float (&v)[32], const PendingParts& p, size_t row, int lane) {
+  if (p.nparts <= 0) return;
+  float ps[32];
+  const float4* q = reinterpret_cast<const float4*>(p.parts + row * HID);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 f = __ldcs(q + i * 32 + lane);
+    ps[4 * i] = f.x; ps[4 * i + 1] = f.y; ps[4 * i + 2] = f.z; ps[4 * i + 3] = f.w;
+  }
+#pragma unroll 1
+  for (int s = 1; s < p.nparts; ++s) {
+    const float4* r = reinterpret_cast<const float4*>(p.parts + static_cast<size_t>(s) * p.stride + row * HID);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = __ldcs(r + i * 32 + lane);
+      ps[4 * i] += f.x; ps[4 * i + 1] += f.y; ps[4 * i + 2] += f.z; ps[4 * i + 3] += f.w;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] += ps[i];
+}
+
 __global__ void __launch_bounds__(256) embed_ln_kernel(const __half* emb, const int* tok, const float* w,
                                                        float eps, float* x, __half* t16, int rows) {
   grid_dep_wait();
@@ -133,10 +159,45 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const int* idx,
   store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
 }
 
+// The residual add of a split-K GEMM (x += its parts) fused with the
+// LayerNorm that follows it.
+__global__ void __launch_bounds__(256) ln_parts_kernel(float* x, const PendingParts p, const float* w,
+                                                       const float* b, float eps, __half* t16, int rows) {
+  grid_dep_wait();
+  grid_dep_trigger();
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float* xr = x + static_cast<size_t>(row) * HID;
+  float v[32];
+  load_f32(xr, lane, v);
+  add_parts(v, p, static_cast<size_t>(row), lane);
+  store_f32(xr, lane, v);
+  normalize(v, eps);
+  scale_shift(v, lane, w, b);
+  store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
+}
+
+// x += parts alone, for a reader of the residual stream that is not a
+// LayerNorm (taps, a single layer run on its own); the same arithmetic as
+// ln_parts_kernel's first half.
+__global__ void __launch_bounds__(256) add_parts_kernel(float* x, const PendingParts p, int rows) {
+  grid_dep_wait();
+  grid_dep_trigger();
+  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float* xr = x + static_cast<size_t>(row) * HID;
+  float v[32];
+  load_f32(xr, lane, v);
+  add_parts(v, p, static_cast<size_t>(row), lane);
+  store_f32(xr, lane, v);
+}
+
 __global__ void __launch_bounds__(256) final_ln_kernel(float* x, const float* wf, const __half* type_emb,
                                                        const uint8_t* rowtype, const float* w1,
                                                        const float* b1, float eps, __half* t16,
-                                                       int rows) {
+                                                       int rows, const PendingParts p) {
   grid_dep_wait();
   grid_dep_trigger();
   const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
@@ -145,6 +206,7 @@ __global__ void __launch_bounds__(256) final_ln_kernel(float* x, const float* wf
   float* xr = x + static_cast<size_t>(row) * HID;
   float v[32], te[32];
   load_f32(xr, lane, v);
+  add_parts(v, p, static_cast<size_t>(row), lane);
   normalize(v, eps);
   scale_shift(v, lane, wf, nullptr);
   load_f16(type_emb + static_cast<size_t>(rowtype[row]) * HID, lane, te);
@@ -180,12 +242,27 @@ cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, 
                     static_cast<const int*>(nullptr), w, static_cast<const float*>(nullptr), eps, t16, x, rows);
 }
 
+cudaError_t launch_ln_parts(float* x, const PendingParts& p, const float* w, const float* b, float eps,
+                            __half* t16, int rows, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID) return cudaErrorInvalidValue;
+  return launch_pdl(ln_parts_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, w, b, eps, t16,
+                    rows);
+}
+
+cudaError_t launch_add_parts(float* x, const PendingParts& p, int rows, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID) return cudaErrorInvalidValue;
+  return launch_pdl(add_parts_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, rows);
+}
+
 cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb, const uint8_t* rowtype,
                             const float* w1, const float* b1, float eps, __half* t16, int rows,
-                            cudaStream_t s) {
+                            cudaStream_t s, const PendingParts& p) {
   if (rows <= 0) return cudaSuccess;
+  if (p.nparts > 0 && (!p.parts || p.stride < static_cast<size_t>(rows) * HID)) return cudaErrorInvalidValue;
   return launch_pdl(final_ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, wf, type_emb, rowtype,
-                    w1, b1, eps, t16, rows);
+                    w1, b1, eps, t16, rows, p);
 }
 
 }  // namespace laya
