@@ -225,6 +225,18 @@ bool splitk_enabled() {
   return on;
 }
 
+// Most K parts per GEMM (LAYA_SPLITK_MAX, 2..8; default 4: on the 179-token
+// request 4 and 8 parts measured the same, 1.98 ms, and 4 reads half the
+// parts back).
+int splitk_max() {
+  static const int n = [] {
+    const char* v = std::getenv("LAYA_SPLITK_MAX");
+    const int k = v ? std::atoi(v) : 4;
+    return k < 2 ? 2 : (k > 8 ? 8 : k);
+  }();
+  return n;
+}
+
 struct HostPlan {
   int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
   std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row, rowseq;
@@ -676,13 +688,13 @@ struct Engine {
 
   // K parts for a residual GEMM of M rows: 1 (no split) unless its tiles
   // fill at most half the clusters; then as many as fill the clusters, at
-  // least 4 k-blocks each, at most 8, within the part region.
+  // least 4 k-blocks each, at most splitk_max(), within the part region.
   int choose_splits(int M, int K) const {
     if (!parts_ready) return 1;
     const int num_m = (M + kGemmBM - 1) / kGemmBM, tiles = num_m * (H / kGemmBN);
     const int clusters = num_sms / 2;
     if (tiles == 0 || tiles * 2 > clusters) return 1;
-    int S = std::min(std::min(clusters / tiles, (K / kGemmBK) / 4), 8);
+    int S = std::min(std::min(clusters / tiles, (K / kGemmBK) / 4), splitk_max());
     while (S > 1 && S * num_m * kGemmBM > kPartRows) --S;
     return S;
   }

@@ -159,8 +159,47 @@ __global__ void __launch_bounds__(256) ln_kernel(const float* x, const int* idx,
   store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
 }
 
-// The residual add of a split-K GEMM (x += its parts) fused with the
+// A streaming 16-byte load kept in program order with the others (volatile),
+// so a batch of them is in flight before the first sum needs one.
+__device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
+  float4 f;
+  asm volatile("ld.global.cs.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w) : "l"(p));
+  return f;
+}
+
+// add_parts with the part count known at compile time: the loads of G
+// float4 chunks of every part are issued together (32 loads in flight per
+// lane), then summed in add_parts' order, element by element.
+template <int NP>
+__device__ __forceinline__ void add_parts_static(float (&v)[32], const PendingParts& p, size_t row, int lane) {
+  constexpr int G = 32 / NP >= 8 ? 8 : 32 / NP;
+  const float4* q = reinterpret_cast<const float4*>(p.parts + row * HID);
+  const size_t st4 = p.stride / 4;
+#pragma unroll
+  for (int i0 = 0; i0 < 8; i0 += G) {
+    float4 f[G][NP];
+#pragma unroll
+    for (int i = 0; i < G; ++i)
+#pragma unroll
+      for (int s = 0; s < NP; ++s)
+        if (i0 + i < 8) f[i][s] = ld_stream_f4(q + s * st4 + (i0 + i) * 32 + lane);
+#pragma unroll
+    for (int i = 0; i < G; ++i) {
+      if (i0 + i >= 8) continue;
+      float4 a = f[i][0];
+#pragma unroll
+      for (int s = 1; s < NP; ++s) {
+        a.x += f[i][s].x; a.y += f[i][s].y; a.z += f[i][s].z; a.w += f[i][s].w;
+      }
+      const int c = 4 * (i0 + i);
+      v[c] += a.x; v[c + 1] += a.y; v[c + 2] += a.z; v[c + 3] += a.w;
+    }
+  }
+}
+
+// The residual add of a split-K GEMM (x += its NP parts) fused with the
 // LayerNorm that follows it.
+template <int NP>
 __global__ void __launch_bounds__(256) ln_parts_kernel(float* x, const PendingParts p, const float* w,
                                                        const float* b, float eps, __half* t16, int rows) {
   grid_dep_wait();
@@ -171,7 +210,7 @@ __global__ void __launch_bounds__(256) ln_parts_kernel(float* x, const PendingPa
   float* xr = x + static_cast<size_t>(row) * HID;
   float v[32];
   load_f32(xr, lane, v);
-  add_parts(v, p, static_cast<size_t>(row), lane);
+  add_parts_static<NP>(v, p, static_cast<size_t>(row), lane);
   store_f32(xr, lane, v);
   normalize(v, eps);
   scale_shift(v, lane, w, b);
@@ -242,12 +281,29 @@ cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, 
                     static_cast<const int*>(nullptr), w, static_cast<const float*>(nullptr), eps, t16, x, rows);
 }
 
+template <int NP>
+cudaError_t launch_ln_parts_n(float* x, const PendingParts& p, const float* w, const float* b, float eps,
+                              __half* t16, int rows, cudaStream_t s) {
+  return launch_pdl(ln_parts_kernel<NP>, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, w, b, eps, t16,
+                    rows);
+}
+
 cudaError_t launch_ln_parts(float* x, const PendingParts& p, const float* w, const float* b, float eps,
                             __half* t16, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID) return cudaErrorInvalidValue;
-  return launch_pdl(ln_parts_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, w, b, eps, t16,
-                    rows);
+  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID || p.stride % 4)
+    return cudaErrorInvalidValue;
+  switch (p.nparts) {
+    case 1: return launch_ln_parts_n<1>(x, p, w, b, eps, t16, rows, s);
+    case 2: return launch_ln_parts_n<2>(x, p, w, b, eps, t16, rows, s);
+    case 3: return launch_ln_parts_n<3>(x, p, w, b, eps, t16, rows, s);
+    case 4: return launch_ln_parts_n<4>(x, p, w, b, eps, t16, rows, s);
+    case 5: return launch_ln_parts_n<5>(x, p, w, b, eps, t16, rows, s);
+    case 6: return launch_ln_parts_n<6>(x, p, w, b, eps, t16, rows, s);
+    case 7: return launch_ln_parts_n<7>(x, p, w, b, eps, t16, rows, s);
+    case 8: return launch_ln_parts_n<8>(x, p, w, b, eps, t16, rows, s);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_add_parts(float* x, const PendingParts& p, int rows, cudaStream_t s) {
