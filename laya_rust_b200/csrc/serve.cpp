@@ -508,6 +508,10 @@ struct Server {
         if (!c.fill(started ? kReadMs : kIdleMs)) return;
         started = true;
       }
+      if (end - c.pos > kMaxHead) {  // the whole head may have come in one read
+        respond(c, 400, error_body("request head too large"), false);
+        return;
+      }
       const auto t0 = std::chrono::steady_clock::now();
       const std::string head = c.buf.substr(c.pos, end - c.pos);
       c.pos = end + 4;

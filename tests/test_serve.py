@@ -299,3 +299,25 @@ def test_cli_rejects_bad_flags(capsys):
     with pytest.raises(SystemExit):
         S.main(["--model", "x.gguf", "--queue", "0"])
     assert S.main(["--model", "/nonexistent.gguf", "--addr", "127.0.0.1:0"]) == 2
+
+
+def test_http_framing_edge_cases(srv, otok, words):
+    a = srv.address
+    body = request_bodies(words, 1, seed=41)[0].encode()
+    want = expected(otok, body.decode()).encode()
+    req = b"POST /systemone HTTP/1.1\r\nContent-Length: %d\r\n\r\n%s" % (len(body), body)
+    # two pipelined requests on one connection, then close
+    out = raw(a, req + req[:-len(body)].replace(b"HTTP/1.1\r\n", b"HTTP/1.1\r\nConnection: close\r\n") + body)
+    assert out.count(b"HTTP/1.1 200 ") == 2 and out.count(want) == 2
+    # HTTP/1.0 closes after the answer unless asked to keep the connection
+    out = raw(a, req.replace(b"HTTP/1.1", b"HTTP/1.0"))
+    assert out.startswith(b"HTTP/1.1 200 ") and b"Connection: close" in out and out.endswith(want)
+    # malformed request line, unknown version, oversized head: 400 and close
+    for bad in (b"POST\r\n\r\n", b"POST /systemone HTTP/2.0\r\n\r\n",
+                b"POST /systemone HTTP/1.1\r\nX: " + b"y" * (70 * 1024) + b"\r\n\r\n",
+                b"POST /systemone HTTP/1.1\r\nContent-Length: 1x\r\n\r\n"):
+        out = raw(a, bad)
+        assert out.startswith(b"HTTP/1.1 400 ") and b"Connection: close" in out, bad[:40]
+    # a 404 without a body keeps the connection open for the next request
+    out = raw(a, b"GET /nope HTTP/1.1\r\n\r\n" + req.replace(b"HTTP/1.1\r\n", b"HTTP/1.1\r\nConnection: close\r\n"))
+    assert out.startswith(b"HTTP/1.1 404 ") and out.count(b"HTTP/1.1 200 ") == 1 and out.endswith(want)
