@@ -20,6 +20,9 @@ namespace {
 constexpr int HID = 1024;
 constexpr int AIN = HID + 4;
 constexpr int AH = 256;
+constexpr int kRowsPerPass = 4;  // W1 rows a warp reads together
+constexpr int kTailThreads = 512;
+static_assert(AIN % 4 == 0 && AH % (kRowsPerPass * (kTailThreads / 32)) == 0, "act head tiling");
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -27,7 +30,7 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-__global__ void __launch_bounds__(256) tail_kernel(const TailArgs a) {
+__global__ void __launch_bounds__(kTailThreads) tail_kernel(const TailArgs a) {
   extern __shared__ float sm[];
   float* ain = sm;             // [1028]
   float* hid = sm + AIN;       // [256]
@@ -82,12 +85,44 @@ __global__ void __launch_bounds__(256) tail_kernel(const TailArgs a) {
     ain[HID + 3] = nn / 255.0f;
   }
   __syncthreads();
-  for (int o = warp; o < AH; o += blockDim.x / 32) {
-    const __half* w = a.w1 + static_cast<size_t>(o) * AIN;
-    float s = 0.0f;
-    for (int i = lane; i < AIN; i += 32) s += __half2float(w[i]) * ain[i];
-    s = warp_sum(s);
-    if (lane == 0) hid[o] = gelu_erf(s + a.b1[o]);
+  // act hidden layer: each warp takes kRowsPerPass rows of W1 at a time and
+  // loads all of them (8-byte pieces: a row is 2056 bytes, 8-byte aligned)
+  // before it sums, so a warp has kRowsPerPass x 9 loads in flight instead
+  // of one row's dependent chain
+  const int nwarps = blockDim.x >> 5;
+  for (int o0 = warp * kRowsPerPass; o0 < AH; o0 += nwarps * kRowsPerPass) {
+    constexpr int kIters = (AIN / 4 + 31) / 32;  // 9 pieces per lane per row
+    uint2 wv[kRowsPerPass][kIters];
+#pragma unroll
+    for (int it = 0; it < kIters; ++it) {
+      const int i4 = lane + 32 * it;
+#pragma unroll
+      for (int r = 0; r < kRowsPerPass; ++r)
+        wv[r][it] = i4 < AIN / 4
+                        ? __ldg(reinterpret_cast<const uint2*>(a.w1 + static_cast<size_t>(o0 + r) * AIN) + i4)
+                        : make_uint2(0u, 0u);
+    }
+    float s[kRowsPerPass];
+#pragma unroll
+    for (int r = 0; r < kRowsPerPass; ++r) s[r] = 0.0f;
+#pragma unroll
+    for (int it = 0; it < kIters; ++it) {
+      const int i4 = lane + 32 * it;
+      if (i4 < AIN / 4) {
+        const float4 x = *reinterpret_cast<const float4*>(ain + 4 * i4);
+#pragma unroll
+        for (int r = 0; r < kRowsPerPass; ++r) {
+          const float2 w01 = __half22float2(*reinterpret_cast<const __half2*>(&wv[r][it].x));
+          const float2 w23 = __half22float2(*reinterpret_cast<const __half2*>(&wv[r][it].y));
+          s[r] += w01.x * x.x + w01.y * x.y + w23.x * x.z + w23.y * x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRowsPerPass; ++r) {
+      const float t = warp_sum(s[r]);
+      if (lane == 0) hid[o0 + r] = gelu_erf(t + a.b1[o0 + r]);
+    }
   }
   __syncthreads();
   if (warp < 2) {
@@ -105,7 +140,7 @@ cudaError_t launch_tail(const TailArgs& a, cudaStream_t s) {
   if (a.n <= 0) return cudaSuccess;
   const size_t smem = sizeof(float) * (AIN + AH + a.k);
   if (smem > 48 * 1024) return cudaErrorInvalidValue;
-  return launch_pdl(tail_kernel, dim3(a.n), dim3(256), smem, s, nullptr, 0, a);
+  return launch_pdl(tail_kernel, dim3(a.n), dim3(kTailThreads), smem, s, nullptr, 0, a);
 }
 
 }  // namespace laya
