@@ -70,6 +70,12 @@ int laya_requests_question(const laya_requests *r, int64_t i, int64_t *request, 
 /* Its token ids [seq_len] and marker positions [n_markers]. */
 int laya_requests_question_tokens(const laya_requests *r, int64_t i, int64_t *seq, int64_t *markers);
 
+/* Moves the requests of parts[0..n_parts) -- planned by separate
+ * laya_requests_plan calls, e.g. one per connection thread -- into one new
+ * object, in that order (request j of part p follows all requests of parts
+ * 0..p-1).  The parts are left with no requests and must still be closed.
+ * Packing, calibration and scores of the new object start fresh. */
+int laya_requests_merge(laya_requests *const *parts, int64_t n_parts, laya_requests **out);
 /* Groups the questions into forwards of at most max_tokens padded tokens
  * (max_len x rows).  across_requests = 0: per request with group_by_budget
  * (questions sorted by length), the reference's run_all; 1: in dispatch

@@ -18,6 +18,7 @@
  *                                      UTF-8
  *       400 {"error":"invalid json: ..."}
  *       503 {"error":"server busy"}    the queue holds `queue` requests already
+ *                                      (counting those still being planned)
  *       422 {"error":"..."}            parse_request / plan_items failed, or
  *                                      {"error":"no questions"}
  *                                      (Service::run, main.rs:1029-1037)
@@ -32,7 +33,9 @@
  *     created on the thread that runs it and never leaves it (the
  *     `laya-infer` thread, main.rs:1151-1160);
  *   - connection threads hand requests over a bounded queue and block for
- *     the answer; a full queue answers 503 rather than buffering.
+ *     the answer; a full queue answers 503 rather than buffering.  Here they
+ *     also plan their request (tokenizer, sequence layout) before queueing
+ *     it, so planning runs on many threads while the GPUs work.
  * What it adds: one inference thread and engine per listed device, all
  * taking requests off the one queue (request-level data parallelism over
  * GPUs, no collective), and optionally `batch` > 1, which lets an inference

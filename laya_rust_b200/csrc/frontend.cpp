@@ -902,6 +902,34 @@ int laya_requests_question_tokens(const laya_requests* r, int64_t i, int64_t* se
   });
 }
 
+int laya_requests_merge(laya_requests* const* parts, int64_t n_parts, laya_requests** out) {
+  return guard([&] {
+    if (!out || n_parts < 0 || (n_parts > 0 && !parts)) throw Error(LAYA_E_INVALID, "null argument");
+    for (int64_t p = 0; p < n_parts; ++p)
+      if (!parts[p]) throw Error(LAYA_E_INVALID, "null part");
+    auto h = std::make_unique<laya_requests>();
+    auto& R = h->r;
+    for (int64_t p = 0; p < n_parts; ++p) {
+      auto& P = parts[p]->r;
+      const int64_t rbase = static_cast<int64_t>(R.reqs.size()), ibase = static_cast<int64_t>(R.items.size());
+      for (auto& it : P.items) {
+        it.request += rbase;
+        it.scored = false;
+        it.ans = laya::json::Value();
+        R.items.push_back(std::move(it));
+      }
+      for (auto& rq : P.reqs) {
+        for (auto& i : rq.items) i += ibase;
+        R.reqs.push_back(std::move(rq));
+      }
+      P.reqs.clear();
+      P.items.clear();
+      P.forwards.clear();
+    }
+    *out = h.release();
+  });
+}
+
 int laya_requests_pack(laya_requests* r, int64_t max_tokens, int across_requests, int64_t* n_forwards) {
   return guard([&] {
     if (!r || !n_forwards || max_tokens <= 0) throw Error(LAYA_E_INVALID, "bad argument");

@@ -2,16 +2,21 @@
 // laya-rust src/main.rs:996-1204 over this library's engines and front end.
 //
 // Threads
-//   - one inference thread per device: it opens its engine itself (the
-//     engine never leaves that thread, main.rs:1151-1160), then takes jobs
-//     off the shared bounded queue, plans them (laya_requests_plan), runs
-//     their forwards, scores them and answers (Service::run, main.rs:1029-1037);
 //   - `connections` connection threads: each accepts a connection and serves
 //     its requests in turn (HTTP/1.1 keep-alive), checking them in the order
-//     of serve_request (main.rs:1072-1138) and blocking on the job's answer.
-// The queue holds at most `queue` jobs that no inference thread has taken
-// (sync_channel(queue), main.rs:1148); a request that finds it full is
-// answered 503 at once.
+//     of serve_request (main.rs:1072-1138); a request that passes takes a
+//     queue slot, is planned on this thread (parse_request + plan_items of
+//     Service::run, main.rs:1029-1034: 422 on failure) and queued, and the
+//     thread blocks on its answer.  Planning here, on many threads, keeps it
+//     off the inference threads' path to the GPU;
+//   - one inference thread per device: it opens its engine itself (the
+//     engine never leaves that thread, main.rs:1151-1160), then takes jobs
+//     off the shared bounded queue (up to `batch`, merged into one set),
+//     packs them, runs their forwards, scores them and answers
+//     (run_all + response, main.rs:520-557).
+// The queue holds at most `queue` jobs that no inference thread has taken,
+// counting those still being planned (sync_channel(queue), main.rs:1148); a
+// request that finds it full is answered 503 at once.
 #include <arpa/inet.h>
 #include <fcntl.h>
 #include <netdb.h>
@@ -69,7 +74,7 @@ std::string error_body(const std::string& msg) {
 
 // One request handed from a connection thread to an inference thread.
 struct Job {
-  std::string body;
+  laya_requests* plan = nullptr;  // one planned request; the inference thread closes it
   int status = 0;
   std::string out;
   bool done = false;
@@ -95,6 +100,9 @@ struct Job {
   void wait() {
     std::unique_lock<std::mutex> g(m);
     cv.wait(g, [&] { return done; });
+  }
+  ~Job() {
+    if (plan) laya_requests_close(plan);
   }
 };
 
@@ -259,6 +267,7 @@ struct Server {
   std::mutex qm;
   std::condition_variable qcv;
   std::deque<std::shared_ptr<Job>> q;
+  int64_t reserved = 0;  // slots held by requests their connection thread is planning
   bool q_closed = false;
 
   std::mutex rm;
@@ -347,34 +356,28 @@ struct Server {
           jobs[j]->finish(code, error_body(msg));
         }
     };
-    std::vector<const char*> texts(n);
-    std::vector<size_t> lens(n);
-    for (int64_t j = 0; j < n; ++j) {
-      texts[j] = jobs[j]->body.data();
-      lens[j] = jobs[j]->body.size();
-    }
+    // the connection threads planned each request; one object for the set
     laya_requests* r = nullptr;
-    if (laya_requests_plan(tok, texts.data(), lens.data(), n, 1, &r) != LAYA_OK ||
-        laya_requests_set_calibration(r, temperature, by_options.c_str()) != LAYA_OK) {
-      fail_open(500, std::string("inference failed: ") + laya_last_error());
-      if (r) laya_requests_close(r);
-      return;
-    }
-    std::vector<int64_t> questions(n, 0);
-    const int64_t nq = laya_requests_questions(r);
-    for (int64_t i = 0; i < nq; ++i) {
-      int64_t req = 0, len = 0, k = 0, qt = 0;
-      if (laya_requests_question(r, i, &req, &len, &k, &qt) == LAYA_OK && req >= 0 && req < n) ++questions[req];
-    }
-    for (int64_t j = 0; j < n; ++j) {
-      // parse_request / plan_items errors, then the empty request: 422
-      if (const char* e = laya_requests_error(r, j)) {
-        open[j] = false;
-        jobs[j]->finish(422, error_body(e));
-      } else if (questions[j] == 0) {
-        open[j] = false;
-        jobs[j]->finish(422, error_body("no questions"));
+    if (n == 1) {
+      r = jobs[0]->plan;
+      jobs[0]->plan = nullptr;
+    } else {
+      std::vector<laya_requests*> parts(n);
+      for (int64_t j = 0; j < n; ++j) parts[j] = jobs[j]->plan;
+      const int st = laya_requests_merge(parts.data(), n, &r);
+      for (int64_t j = 0; j < n; ++j) {
+        laya_requests_close(jobs[j]->plan);
+        jobs[j]->plan = nullptr;
       }
+      if (st != LAYA_OK) {
+        fail_open(500, std::string("inference failed: ") + laya_last_error());
+        return;
+      }
+    }
+    if (laya_requests_set_calibration(r, temperature, by_options.c_str()) != LAYA_OK) {
+      fail_open(500, std::string("inference failed: ") + laya_last_error());
+      laya_requests_close(r);
+      return;
     }
     int64_t nf = 0;
     if (laya_requests_pack(r, max_tokens, n > 1 ? 1 : 0, &nf) != LAYA_OK) {
@@ -619,22 +622,58 @@ struct Server {
         if (keep) continue;
         return;
       }
-      auto job = std::make_shared<Job>();
-      job->body = std::move(body);
+      // a queue slot first (a full queue answers 503 before the request is
+      // looked at, as in the reference), then parse_request + plan_items on
+      // this thread, so the inference threads only pack and run forwards
       int busy = 0;
       {
         std::lock_guard<std::mutex> g(qm);
         if (q_closed)
           busy = 1;
-        else if (static_cast<int64_t>(q.size()) >= queue_cap)
+        else if (static_cast<int64_t>(q.size()) + reserved >= queue_cap)
           busy = 2;
         else
-          q.push_back(job);
+          ++reserved;
       }
       if (busy) {
         const std::string m = busy == 1 ? "inference thread stopped" : "server busy";
         respond(c, 503, error_body(m), keep);
         log(503, m);
+        if (keep) continue;
+        return;
+      }
+      auto job = std::make_shared<Job>();
+      int code = 0;
+      std::string why2;
+      {
+        const char* text = body.data();
+        const size_t len = body.size();
+        if (laya_requests_plan(tok, &text, &len, 1, 1, &job->plan) != LAYA_OK) {
+          code = 500;
+          why2 = std::string("inference failed: ") + laya_last_error();
+        } else if (const char* e = laya_requests_error(job->plan, 0)) {
+          code = 422;  // parse_request / plan_items (Service::run, main.rs:1030-1034)
+          why2 = e;
+        } else if (laya_requests_questions(job->plan) == 0) {
+          code = 422;
+          why2 = "no questions";
+        }
+      }
+      {
+        std::lock_guard<std::mutex> g(qm);
+        --reserved;
+        if (!code) {
+          if (q_closed) {
+            code = 503;
+            why2 = "inference thread stopped";
+          } else {
+            q.push_back(job);
+          }
+        }
+      }
+      if (code) {
+        respond(c, code, error_body(why2), keep);
+        log(code, why2);
         if (keep) continue;
         return;
       }

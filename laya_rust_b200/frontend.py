@@ -46,6 +46,7 @@ def lib():
         L.laya_requests_set_calibration.argtypes = [vp, _f32p, ctypes.c_char_p]
         L.laya_requests_score.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
         L.laya_requests_response.argtypes = [vp, ctypes.c_int64, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
+        L.laya_requests_merge.argtypes = [ctypes.POINTER(vp), ctypes.c_int64, ctypes.POINTER(vp)]
         L.laya_requests_close.argtypes = [vp]
         L.laya_requests_close.restype = None
         _bound = True
@@ -109,6 +110,22 @@ class Requests:
         self._h = ctypes.c_void_p()
         _check(lib().laya_requests_plan(tok._h, arr, lens, len(bs), threads, ctypes.byref(self._h)))
         self.n_requests = len(bs)
+
+    @classmethod
+    def merge(cls, parts: list) -> "Requests":
+        """laya_requests_merge: one object holding the requests of `parts`
+        in order (the parts are left empty)."""
+        arr = (ctypes.c_void_p * len(parts))(*[p._h for p in parts])
+        h = ctypes.c_void_p()
+        _check(lib().laya_requests_merge(arr, len(parts), ctypes.byref(h)))
+        self = cls.__new__(cls)
+        self._keep = [b for p in parts for b in p._keep]
+        self._tok = parts[0]._tok if parts else None
+        self._h = h
+        self.n_requests = sum(p.n_requests for p in parts)
+        for p in parts:
+            p.n_requests = 0
+        return self
 
     def error(self, request: int) -> str | None:
         e = lib().laya_requests_error(self._h, request)

@@ -337,3 +337,43 @@ def test_long_pieces_match_and_stay_fast(tok, otok):
     t0 = time.perf_counter()
     ids = tok.encode("stand" * 10000)
     assert time.perf_counter() - t0 < 1.0 and len(ids) > 0
+
+
+def test_merge_of_separately_planned_requests_equals_one_plan(tok, tj):
+    """laya_requests_merge: requests planned one by one (as the HTTP service's
+    connection threads do) pack, score and answer exactly like the same
+    requests planned together; errors stay with their request."""
+    words = workloads.vocab_words(tj)
+    rng = np.random.default_rng(3)
+    reqs = [workloads.system_one_request_json(rng, words, int(rng.integers(10, 120)),
+                                              workloads.random_questions(rng)[:int(rng.integers(1, 6))])
+            for _ in range(5)]
+    reqs.insert(2, {"state": "x"})  # fails to plan
+    texts = [json.dumps(r) for r in reqs]
+    whole = FE.Requests(tok, texts)
+    parts = [FE.Requests(tok, [t]) for t in texts]
+    merged = FE.Requests.merge(parts)
+    assert all(p.n_requests == 0 for p in parts)
+    assert merged.n_requests == whole.n_requests == len(reqs)
+    assert merged.questions() == whole.questions()
+    for i in range(whole.questions()):
+        assert merged.question(i) == whole.question(i)
+    for across in (False, True):
+        nf = whole.pack(4096, across)
+        assert merged.pack(4096, across) == nf
+        for f in range(nf):
+            a, b = whole.batch(f), merged.batch(f)
+            for name in ("ids", "att", "mpos", "mmask", "qtype"):
+                assert np.array_equal(getattr(a, name), getattr(b, name))
+            lg = np.sin(np.arange(a.n * a.k, dtype=np.float32))
+            ac = np.cos(np.arange(a.n * 2, dtype=np.float32))
+            whole.score(f, lg, ac)
+            merged.score(f, lg, ac)
+        for j in range(len(reqs)):
+            assert merged.error(j) == whole.error(j)
+            if whole.error(j) is None:
+                assert merged.response_text(j) == whole.response_text(j)
+    for p in parts:
+        p.close()
+    merged.close()
+    whole.close()
