@@ -80,7 +80,9 @@ int laya_requests_merge(laya_requests *const *parts, int64_t n_parts, laya_reque
  * (max_len x rows).  across_requests = 0: per request with group_by_budget
  * (questions sorted by length), the reference's run_all; 1: in dispatch
  * order across requests (a forward closes when the next question would break
- * the budget).  *n_forwards receives the count. */
+ * the budget); 2: group_by_budget over all the questions of all the requests
+ * (sorted by length, ties in dispatch order), the fewest forwards for a set
+ * whose requests finish together.  *n_forwards receives the count. */
 int laya_requests_pack(laya_requests *r, int64_t max_tokens, int across_requests, int64_t *n_forwards);
 /* Forward f's batch shape. */
 int laya_requests_forward_shape(const laya_requests *r, int64_t f, int64_t *n, int64_t *l, int64_t *k);

@@ -40,8 +40,8 @@
  * taking requests off the one queue (request-level data parallelism over
  * GPUs, no collective), and optionally `batch` > 1, which lets an inference
  * thread take up to `batch` queued requests at once and pack their questions
- * into shared forwards (laya_requests_pack across requests).  batch <= 1 is
- * the reference's run_all per request.
+ * into shared forwards (laya_requests_pack, grouped by length across the
+ * set).  batch <= 1 is the reference's run_all per request.
  *
  * Conventions are those of laya_b200.h: LAYA_OK (0) or a nonzero status with
  * the message in laya_last_error().

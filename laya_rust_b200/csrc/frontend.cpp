@@ -932,7 +932,8 @@ int laya_requests_merge(laya_requests* const* parts, int64_t n_parts, laya_reque
 
 int laya_requests_pack(laya_requests* r, int64_t max_tokens, int across_requests, int64_t* n_forwards) {
   return guard([&] {
-    if (!r || !n_forwards || max_tokens <= 0) throw Error(LAYA_E_INVALID, "bad argument");
+    if (!r || !n_forwards || max_tokens <= 0 || across_requests < 0 || across_requests > 2)
+      throw Error(LAYA_E_INVALID, "bad argument");
     auto& R = r->r;
     R.forwards.clear();
     for (auto& it : R.items) it.scored = false;
@@ -955,6 +956,9 @@ int laya_requests_pack(laya_requests* r, int64_t max_tokens, int across_requests
     if (across_requests) {
       std::vector<int64_t> order(R.items.size());
       for (size_t i = 0; i < order.size(); ++i) order[i] = static_cast<int64_t>(i);
+      if (across_requests == 2)  // group_by_budget over the whole set
+        std::stable_sort(order.begin(), order.end(),
+                         [&](int64_t a, int64_t b) { return R.items[a].seq.size() < R.items[b].seq.size(); });
       close_over(order);
     } else {
       for (const auto& rq : R.reqs) {

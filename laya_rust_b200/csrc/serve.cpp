@@ -380,7 +380,9 @@ struct Server {
       return;
     }
     int64_t nf = 0;
-    if (laya_requests_pack(r, max_tokens, n > 1 ? 1 : 0, &nf) != LAYA_OK) {
+    // one request: run_all's grouping; a set taken together finishes
+    // together, so it is grouped by length as a whole (fewest forwards)
+    if (laya_requests_pack(r, max_tokens, n > 1 ? 2 : 0, &nf) != LAYA_OK) {
       fail_open(500, std::string("inference failed: ") + laya_last_error());
       laya_requests_close(r);
       return;

@@ -157,7 +157,9 @@ class Requests:
         _check(lib().laya_requests_forward_questions(self._h, f, _p64(q)))
         return q[:n.value].tolist()
 
-    def pack(self, max_tokens: int = 16384, across_requests: bool = False) -> int:
+    def pack(self, max_tokens: int = 16384, across_requests: bool | int = False) -> int:
+        """across_requests: 0/False per request (run_all), 1/True dispatch
+        order across requests, 2 sorted by length across requests."""
         n = ctypes.c_int64()
         _check(lib().laya_requests_pack(self._h, max_tokens, int(across_requests), ctypes.byref(n)))
         return n.value

@@ -377,3 +377,31 @@ def test_merge_of_separately_planned_requests_equals_one_plan(tok, tj):
         p.close()
     merged.close()
     whole.close()
+
+
+def test_pack_sorted_across_requests_is_group_by_budget_over_the_set(tok, tj):
+    """across_requests = 2: the reference's group_by_budget (main.rs:448-468)
+    applied to every question of every request at once."""
+    words = workloads.vocab_words(tj)
+    rng = np.random.default_rng(8)
+    reqs = [workloads.system_one_request_json(rng, words, int(rng.integers(10, 300)),
+                                              workloads.random_questions(rng)[:int(rng.integers(1, 8))])
+            for _ in range(12)]
+    rq = FE.Requests(tok, reqs)
+    lens = [rq.question_shape(i)[1] for i in range(rq.questions())]
+    for budget in (2048, 16384):
+        order = sorted(range(len(lens)), key=lambda i: lens[i])  # stable
+        want, cur, cur_max = [], [], 0
+        for i in order:
+            if cur and max(cur_max, lens[i]) * (len(cur) + 1) > budget:
+                want.append(cur)
+                cur, cur_max = [], 0
+            cur_max = max(cur_max, lens[i])
+            cur.append(i)
+        want.append(cur)
+        nf = rq.pack(budget, 2)
+        assert [rq.forward_questions(f) for f in range(nf)] == want
+        assert nf <= rq.pack(budget, 1)
+    with pytest.raises(FE.LayaError):
+        rq.pack(16384, 3)
+    rq.close()
