@@ -77,6 +77,9 @@ def parse():
     ap.add_argument("--config", default="forward-16k", choices=CONFIGS)
     ap.add_argument("--cpu-sample", type=int, default=4, help="sequences in the CPU baseline sample")
     ap.add_argument("--requests", type=int, default=4096, help="requests in the stream configuration")
+    ap.add_argument("--stream-window", type=int, default=64,
+                    help="stream: group questions by length within windows of this many consecutive "
+                         "requests (0: pack in dispatch order)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -697,7 +700,9 @@ def run_stream(args, d, eng):
     """Config 4: the request stream (JSON) through the C++ front end: every
     rank plans all requests on its host threads to learn their token costs,
     takes the share the greedy cost assignment gives it, and packs its
-    questions across requests into <=16384-token forwards."""
+    questions across requests into <=16384-token forwards: grouped by length
+    (group_by_budget) within windows of --stream-window consecutive requests,
+    in dispatch order from window to window."""
     import numpy as np
     from laya_rust_b200 import frontend as FE, modelgen, workloads
     torch = d.torch
@@ -721,7 +726,7 @@ def run_stream(args, d, eng):
     t = time.perf_counter()
     rq = FE.Requests(tok, [texts[i] for i in mine], threads=0)
     plan_s = time.perf_counter() - t
-    nf = rq.pack(16384, True)
+    nf = rq.pack_windows(16384, args.stream_window) if args.stream_window > 0 else rq.pack(16384, True)
     batches = [rq.batch(f) for f in range(nf)]
     fq = [rq.forward_questions(f) for f in range(nf)]
     q_req = [rq.question_shape(i)[0] for i in range(rq.questions())]
@@ -798,6 +803,8 @@ def run_stream(args, d, eng):
     if d.rank == 0:
         cfg = {"workload": "stream", "model": MODEL, "requests": len(texts), "questions": int(questions_all),
                "forwards": int(forwards), "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
+               "packing": (f"group_by_budget within windows of {args.stream_window} requests"
+                           if args.stream_window > 0 else "dispatch order"),
                "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
                "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
         steps = nf

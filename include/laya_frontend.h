@@ -84,6 +84,11 @@ int laya_requests_merge(laya_requests *const *parts, int64_t n_parts, laya_reque
  * (sorted by length, ties in dispatch order), the fewest forwards for a set
  * whose requests finish together.  *n_forwards receives the count. */
 int laya_requests_pack(laya_requests *r, int64_t max_tokens, int across_requests, int64_t *n_forwards);
+/* group_by_budget over each window of `window` consecutive requests in turn
+ * (window 1: laya_requests_pack mode 0; window >= the request count: mode
+ * 2).  A stream served in dispatch order keeps its order between windows
+ * and gets fuller forwards inside each. */
+int laya_requests_pack_windows(laya_requests *r, int64_t max_tokens, int64_t window, int64_t *n_forwards);
 /* Forward f's batch shape. */
 int laya_requests_forward_shape(const laya_requests *r, int64_t f, int64_t *n, int64_t *l, int64_t *k);
 /* The question index of each of forward f's n rows. */

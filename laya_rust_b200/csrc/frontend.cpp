@@ -972,6 +972,38 @@ int laya_requests_pack(laya_requests* r, int64_t max_tokens, int across_requests
   });
 }
 
+int laya_requests_pack_windows(laya_requests* r, int64_t max_tokens, int64_t window, int64_t* n_forwards) {
+  return guard([&] {
+    if (!r || !n_forwards || max_tokens <= 0 || window <= 0) throw Error(LAYA_E_INVALID, "bad argument");
+    auto& R = r->r;
+    R.forwards.clear();
+    for (auto& it : R.items) it.scored = false;
+    const int64_t nreq = static_cast<int64_t>(R.reqs.size());
+    for (int64_t w0 = 0; w0 < nreq; w0 += window) {
+      // group_by_budget (main.rs:448-468) over the window's questions
+      std::vector<int64_t> order;
+      for (int64_t q = w0; q < std::min(nreq, w0 + window); ++q)
+        order.insert(order.end(), R.reqs[q].items.begin(), R.reqs[q].items.end());
+      std::stable_sort(order.begin(), order.end(),
+                       [&](int64_t a, int64_t b) { return R.items[a].seq.size() < R.items[b].seq.size(); });
+      std::vector<int64_t> cur;
+      size_t cur_max = 0;
+      for (const int64_t i : order) {
+        const size_t ln = R.items[i].seq.size();
+        if (!cur.empty() && std::max(cur_max, ln) * (cur.size() + 1) > static_cast<size_t>(max_tokens)) {
+          R.forwards.push_back(std::move(cur));
+          cur.clear();
+          cur_max = 0;
+        }
+        cur_max = std::max(cur_max, ln);
+        cur.push_back(i);
+      }
+      if (!cur.empty()) R.forwards.push_back(std::move(cur));
+    }
+    *n_forwards = static_cast<int64_t>(R.forwards.size());
+  });
+}
+
 int laya_requests_forward_shape(const laya_requests* r, int64_t f, int64_t* n, int64_t* l, int64_t* k) {
   return guard([&] {
     if (!r || f < 0 || f >= static_cast<int64_t>(r->r.forwards.size())) throw Error(LAYA_E_INVALID, "forward out of range");

@@ -47,6 +47,7 @@ def lib():
         L.laya_requests_score.argtypes = [vp, ctypes.c_int64, _f32p, _f32p]
         L.laya_requests_response.argtypes = [vp, ctypes.c_int64, ctypes.c_char_p, sz, ctypes.POINTER(sz)]
         L.laya_requests_merge.argtypes = [ctypes.POINTER(vp), ctypes.c_int64, ctypes.POINTER(vp)]
+        L.laya_requests_pack_windows.argtypes = [vp, ctypes.c_int64, ctypes.c_int64, _i64p]
         L.laya_requests_close.argtypes = [vp]
         L.laya_requests_close.restype = None
         _bound = True
@@ -162,6 +163,12 @@ class Requests:
         order across requests, 2 sorted by length across requests."""
         n = ctypes.c_int64()
         _check(lib().laya_requests_pack(self._h, max_tokens, int(across_requests), ctypes.byref(n)))
+        return n.value
+
+    def pack_windows(self, max_tokens: int = 16384, window: int = 64) -> int:
+        """group_by_budget over each window of `window` consecutive requests."""
+        n = ctypes.c_int64()
+        _check(lib().laya_requests_pack_windows(self._h, max_tokens, window, ctypes.byref(n)))
         return n.value
 
     def batch(self, f: int) -> Req:

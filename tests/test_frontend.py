@@ -405,3 +405,32 @@ def test_pack_sorted_across_requests_is_group_by_budget_over_the_set(tok, tj):
     with pytest.raises(FE.LayaError):
         rq.pack(16384, 3)
     rq.close()
+
+
+def test_pack_windows_is_group_by_budget_per_window(tok, tj):
+    """laya_requests_pack_windows: window 1 is run_all's per-request
+    grouping (mode 0), a window over every request is mode 2, and in between
+    each window of consecutive requests is grouped on its own."""
+    words = workloads.vocab_words(tj)
+    rng = np.random.default_rng(12)
+    reqs = [workloads.system_one_request_json(rng, words, int(rng.integers(10, 300)),
+                                              workloads.random_questions(rng)[:int(rng.integers(1, 8))])
+            for _ in range(11)]
+    rq = FE.Requests(tok, reqs)
+    fw = lambda nf: [rq.forward_questions(f) for f in range(nf)]
+    assert fw(rq.pack_windows(4096, 1)) == fw(rq.pack(4096, 0))
+    assert fw(rq.pack_windows(4096, 11)) == fw(rq.pack(4096, 2))
+    assert fw(rq.pack_windows(4096, 100)) == fw(rq.pack(4096, 2))
+    got = fw(rq.pack_windows(4096, 4))
+    owner = [rq.question_shape(i)[0] for i in range(rq.questions())]
+    want = []
+    for w0 in range(0, 11, 4):
+        part = FE.Requests(tok, reqs[w0:w0 + 4])
+        base = sum(1 for o in owner if o < w0)  # questions of the earlier requests
+        for f in range(part.pack(4096, 2)):
+            want.append([q + base for q in part.forward_questions(f)])
+        part.close()
+    assert got == want
+    with pytest.raises(FE.LayaError):
+        rq.pack_windows(4096, 0)
+    rq.close()
