@@ -17,7 +17,8 @@
  * Numerics follow the reference exactly: f32 tensors, f64 layer-norm
  * statistics, Abramowitz & Stegun 7.1.26 erf in f64, k-outer f32 GEMM
  * (gemm_nt) and per-output dot products (gemm_t), rows split across
- * LAYA_CPU_THREADS threads, single-threaded attention, glibc expf/logf/cosf/
+ * LAYA_CPU_THREADS threads, single-threaded attention (tests may spread its
+ * (sequence, head) pairs over threads: same results), glibc expf/logf/cosf/
  * sinf/powf (what Rust's f32 methods call on linux-gnu).  Build without
  * -ffast-math and with -ffp-contract=off so no multiply-add is fused.
  *
@@ -271,43 +272,87 @@ void lo_split_qkv_rope(const float *qkv, size_t rows, const float *cosb, const f
             }
 }
 
+/* attention for one (sequence b, head h): cpu/mod.rs:257-314 */
+static void attn_one(const float *q, const float *k, const float *v, const float *mask, size_t b, size_t h,
+                     size_t nh, size_t len, size_t hd, float *scores, float *out) {
+    size_t head = ((b * nh + h) * len) * hd;
+    const float *qb = q + head, *kb = k + head, *vb = v + head;
+    const float *mb = mask + b * len * len;
+    for (size_t s = 0; s < len; s++) {
+        const float *qs = qb + s * hd;
+        const float *ms = mb + s * len;
+        float mx = -3.4e38f;
+        for (size_t t = 0; t < len; t++) {
+            const float *kt = kb + t * hd;
+            float acc = 0.0f;
+            for (size_t d = 0; d < hd; d++) acc += qs[d] * kt[d];
+            float sc = acc + ms[t];
+            scores[t] = sc;
+            if (sc > mx) mx = sc;
+        }
+        float sum = 0.0f;
+        for (size_t t = 0; t < len; t++) {
+            float e = expf(scores[t] - mx);
+            scores[t] = e;
+            sum += e;
+        }
+        float inv = 1.0f / sum;
+        for (size_t t = 0; t < len; t++) scores[t] *= inv;
+        for (size_t d = 0; d < hd; d++) {
+            float acc = 0.0f;
+            for (size_t t = 0; t < len; t++) acc += scores[t] * vb[t * hd + d];
+            out[(b * len + s) * nh * hd + h * hd + d] = acc;
+        }
+    }
+}
+
+typedef struct {
+    const float *q, *k, *v, *mask;
+    size_t nh, len, hd, p0, p1;
+    float *out;
+} attn_job;
+
+static void *attn_worker(void *arg) {
+    attn_job *j = (attn_job *)arg;
+    float *scores = (float *)malloc(sizeof(float) * (j->len ? j->len : 1));
+    for (size_t p = j->p0; p < j->p1; p++)
+        attn_one(j->q, j->k, j->v, j->mask, p / j->nh, p % j->nh, j->nh, j->len, j->hd, scores, j->out);
+    free(scores);
+    return NULL;
+}
+
+/* Test infrastructure may set LAYA_ORACLE_THREADED_ATTENTION=1: the
+ * (sequence, head) pairs are then split across LAYA_CPU_THREADS threads.
+ * Every output element is computed by the same code either way, so the
+ * results are identical; the timed CPU baseline keeps the reference's single
+ * thread. */
+static int lo_threaded_attention(void) {
+    const char *v = getenv("LAYA_ORACLE_THREADED_ATTENTION");
+    return v && v[0] == '1';
+}
+
 /* attention: q,k,v [n, nh, len, hd], mask [n, len, len] -> out [n*len, nh*hd] */
 void lo_attention(const float *q, const float *k, const float *v, const float *mask, size_t n,
                   size_t nh, size_t len, size_t hd, float *out) {
-    float *scores = (float *)malloc(sizeof(float) * (len ? len : 1));
-    for (size_t b = 0; b < n; b++)
-        for (size_t h = 0; h < nh; h++) {
-            size_t head = ((b * nh + h) * len) * hd;
-            const float *qb = q + head, *kb = k + head, *vb = v + head;
-            const float *mb = mask + b * len * len;
-            for (size_t s = 0; s < len; s++) {
-                const float *qs = qb + s * hd;
-                const float *ms = mb + s * len;
-                float mx = -3.4e38f;
-                for (size_t t = 0; t < len; t++) {
-                    const float *kt = kb + t * hd;
-                    float acc = 0.0f;
-                    for (size_t d = 0; d < hd; d++) acc += qs[d] * kt[d];
-                    float sc = acc + ms[t];
-                    scores[t] = sc;
-                    if (sc > mx) mx = sc;
-                }
-                float sum = 0.0f;
-                for (size_t t = 0; t < len; t++) {
-                    float e = expf(scores[t] - mx);
-                    scores[t] = e;
-                    sum += e;
-                }
-                float inv = 1.0f / sum;
-                for (size_t t = 0; t < len; t++) scores[t] *= inv;
-                for (size_t d = 0; d < hd; d++) {
-                    float acc = 0.0f;
-                    for (size_t t = 0; t < len; t++) acc += scores[t] * vb[t * hd + d];
-                    out[(b * len + s) * nh * hd + h * hd + d] = acc;
-                }
-            }
-        }
-    free(scores);
+    const size_t pairs = n * nh;
+    size_t nt = lo_threaded_attention() ? (size_t)lo_nthreads() : 1;
+    if (nt > pairs) nt = pairs ? pairs : 1;
+    attn_job *jobs = (attn_job *)calloc(nt, sizeof(attn_job));
+    pthread_t *tid = (pthread_t *)calloc(nt, sizeof(pthread_t));
+    const size_t chunk = (pairs + nt - 1) / nt;
+    for (size_t t = 0; t < nt; t++) {
+        attn_job *j = &jobs[t];
+        j->q = q; j->k = k; j->v = v; j->mask = mask;
+        j->nh = nh; j->len = len; j->hd = hd; j->out = out;
+        j->p0 = t * chunk < pairs ? t * chunk : pairs;
+        j->p1 = (t + 1) * chunk < pairs ? (t + 1) * chunk : pairs;
+        if (nt == 1) attn_worker(j);
+        else pthread_create(&tid[t], NULL, attn_worker, j);
+    }
+    if (nt > 1)
+        for (size_t t = 0; t < nt; t++) pthread_join(tid[t], NULL);
+    free(tid);
+    free(jobs);
 }
 
 /* window_mask: window < 0 means "no window" */

@@ -115,6 +115,22 @@ def test_attention_mask_drops_keys():
     assert_close(out, [1.0, 0.0, 1.0 - p, p], 1e-5, "masked attention")
 
 
+def test_threaded_attention_is_bitwise_the_single_threaded_one(monkeypatch):
+    """LAYA_ORACLE_THREADED_ATTENTION splits the (sequence, head) pairs over
+    threads; every output element runs the same code, so nothing changes."""
+    rng = np.random.default_rng(5)
+    n, nh, length, hd = 3, 4, 37, 8
+    q, k, v = (rng.standard_normal((n, nh, length, hd)).astype(np.float32) for _ in range(3))
+    att = np.ones((n, length), np.int64)
+    att[1, 30:] = 0
+    mask = O.window_mask(att, n, length, 5)
+    outs = []
+    for flag in ("0", "1"):
+        monkeypatch.setenv("LAYA_ORACLE_THREADED_ATTENTION", flag)
+        outs.append(O.attention(q, k, v, mask, nh, length))
+    assert outs[0].tobytes() == outs[1].tobytes()
+
+
 def test_window_mask_marks_padding_and_distant_keys():
     """tests/ops.rs:160-180 (exact -3.4e38)"""
     m = O.window_mask([1, 1, 0, 1], 1, 4, None)
