@@ -17,10 +17,15 @@
  * Numerics follow the reference exactly: f32 tensors, f64 layer-norm
  * statistics, Abramowitz & Stegun 7.1.26 erf in f64, k-outer f32 GEMM
  * (gemm_nt) and per-output dot products (gemm_t), rows split across
- * LAYA_CPU_THREADS threads, single-threaded attention (tests may spread its
- * (sequence, head) pairs over threads: same results), glibc expf/logf/cosf/
+ * LAYA_CPU_THREADS threads, single-threaded attention, glibc expf/logf/cosf/
  * sinf/powf (what Rust's f32 methods call on linux-gnu).  Build without
  * -ffast-math and with -ffp-contract=off so no multiply-add is fused.
+ *
+ * LAYA_ORACLE_FAST=1 (set by the test suite, never by the timed CPU
+ * baseline) computes the same values faster: gemm_nt in register tiles and
+ * the attention's (sequence, head) pairs on all threads.  Every output
+ * element keeps the reference's operation sequence; tests check bit
+ * equality with the reference traversal.
  *
  * Parity status: the op functions are pinned by the reference's own op
  * known-answer tests (tests/ops.rs:42-267) and the f16 conversion by
@@ -30,6 +35,9 @@
 #define _GNU_SOURCE
 #include <math.h>
 #include <pthread.h>
+#if defined(__SSE2__)
+#include <emmintrin.h>
+#endif
 #include <stdint.h>
 #include <stdio.h>
 #include <stdlib.h>
@@ -157,6 +165,106 @@ static void *gemm_nt_worker(void *arg) {
     return NULL;
 }
 
+/* Test infrastructure: the same sums as gemm_nt_worker, element by element
+ * (y starts at 0 and adds the rounded a*w over k = 0, 1, ... in order, one
+ * rounding per multiply and per add: SSE2 multiplies and adds, never fused),
+ * computed 4 rows x 8 columns at a time in registers from a copy of the 8
+ * columns of w laid out k-major.  A job is a range of 8-column blocks over
+ * every row, so w is packed once per GEMM. */
+typedef struct {
+    const float *x, *w;
+    float *y;
+    size_t r, kk, n, cb0, cb1;
+} tile_job;
+
+static void *gemm_nt_tiled_worker(void *arg) {
+    tile_job *j = (tile_job *)arg;
+    const size_t r = j->r, kk = j->kk, n = j->n;
+    float *pk = (float *)aligned_alloc(16, ((kk * 8 * sizeof(float) + 15) / 16) * 16 + 16);
+    for (size_t cb = j->cb0; cb < j->cb1; cb++) {
+        const size_t c0 = cb * 8;
+        for (size_t kx = 0; kx < kk; kx++)
+            for (int c = 0; c < 8; c++) pk[kx * 8 + c] = j->w[kx * n + c0 + c];
+        size_t r0 = 0;
+#if defined(__SSE2__)
+        for (; r0 + 4 <= r; r0 += 4) {
+            const float *x0 = j->x + r0 * kk, *x1 = x0 + kk, *x2 = x1 + kk, *x3 = x2 + kk;
+            float *y0 = j->y + r0 * n + c0;
+            __m128 a00 = _mm_loadu_ps(y0), a01 = _mm_loadu_ps(y0 + 4);
+            __m128 a10 = _mm_loadu_ps(y0 + n), a11 = _mm_loadu_ps(y0 + n + 4);
+            __m128 a20 = _mm_loadu_ps(y0 + 2 * n), a21 = _mm_loadu_ps(y0 + 2 * n + 4);
+            __m128 a30 = _mm_loadu_ps(y0 + 3 * n), a31 = _mm_loadu_ps(y0 + 3 * n + 4);
+            const float *wp = pk;
+            for (size_t kx = 0; kx < kk; kx++, wp += 8) {
+                const __m128 w0 = _mm_load_ps(wp), w1 = _mm_load_ps(wp + 4);
+                __m128 b = _mm_set1_ps(x0[kx]);
+                a00 = _mm_add_ps(a00, _mm_mul_ps(b, w0));
+                a01 = _mm_add_ps(a01, _mm_mul_ps(b, w1));
+                b = _mm_set1_ps(x1[kx]);
+                a10 = _mm_add_ps(a10, _mm_mul_ps(b, w0));
+                a11 = _mm_add_ps(a11, _mm_mul_ps(b, w1));
+                b = _mm_set1_ps(x2[kx]);
+                a20 = _mm_add_ps(a20, _mm_mul_ps(b, w0));
+                a21 = _mm_add_ps(a21, _mm_mul_ps(b, w1));
+                b = _mm_set1_ps(x3[kx]);
+                a30 = _mm_add_ps(a30, _mm_mul_ps(b, w0));
+                a31 = _mm_add_ps(a31, _mm_mul_ps(b, w1));
+            }
+            _mm_storeu_ps(y0, a00);
+            _mm_storeu_ps(y0 + 4, a01);
+            _mm_storeu_ps(y0 + n, a10);
+            _mm_storeu_ps(y0 + n + 4, a11);
+            _mm_storeu_ps(y0 + 2 * n, a20);
+            _mm_storeu_ps(y0 + 2 * n + 4, a21);
+            _mm_storeu_ps(y0 + 3 * n, a30);
+            _mm_storeu_ps(y0 + 3 * n + 4, a31);
+        }
+#endif
+        for (; r0 < r; r0++) {
+            float *yr = j->y + r0 * n + c0;
+            for (size_t kx = 0; kx < kk; kx++) {
+                const float a = j->x[r0 * kk + kx];
+                for (int c = 0; c < 8; c++) yr[c] += a * pk[kx * 8 + c];
+            }
+        }
+    }
+    free(pk);
+    return NULL;
+}
+
+static int lo_fast(void) {
+    const char *v = getenv("LAYA_ORACLE_FAST");
+    return v && v[0] == '1';
+}
+
+static void run_gemm_tiled(const float *x, const float *w, float *y, size_t r, size_t kk, size_t n) {
+    memset(y, 0, sizeof(float) * r * n);
+    const size_t nb = n / 8;
+    size_t nt = (size_t)lo_nthreads();
+    if (nt > nb) nt = nb ? nb : 1;
+    tile_job *jobs = (tile_job *)calloc(nt, sizeof(tile_job));
+    pthread_t *tid = (pthread_t *)calloc(nt, sizeof(pthread_t));
+    const size_t chunk = (nb + nt - 1) / nt;
+    for (size_t t = 0; t < nt; t++) {
+        tile_job *j = &jobs[t];
+        j->x = x; j->w = w; j->y = y; j->r = r; j->kk = kk; j->n = n;
+        j->cb0 = t * chunk < nb ? t * chunk : nb;
+        j->cb1 = (t + 1) * chunk < nb ? (t + 1) * chunk : nb;
+        if (nt == 1) gemm_nt_tiled_worker(j);
+        else pthread_create(&tid[t], NULL, gemm_nt_tiled_worker, j);
+    }
+    if (nt > 1)
+        for (size_t t = 0; t < nt; t++) pthread_join(tid[t], NULL);
+    /* the last n % 8 columns, k in order */
+    for (size_t ri = 0; ri < r; ri++)
+        for (size_t kx = 0; kx < kk; kx++) {
+            const float a = x[ri * kk + kx];
+            for (size_t c = nb * 8; c < n; c++) y[ri * n + c] += a * w[kx * n + c];
+        }
+    free(tid);
+    free(jobs);
+}
+
 static void *gemm_t_worker(void *arg) {
     gemm_job *j = (gemm_job *)arg;
     for (size_t r = j->row0; r < j->row1; r++) {
@@ -202,7 +310,14 @@ static void run_gemm(void *(*fn)(void *), const float *x, const float *w, float 
 
 /* matmul: x [r, kk] . w [kk, n]  (w in graph layout, out contiguous) */
 void lo_matmul(const float *x, size_t r, size_t kk, const float *w, size_t n, float *y) {
-    run_gemm(gemm_nt_worker, x, w, y, r, kk, n);
+    if (lo_fast()) run_gemm_tiled(x, w, y, r, kk, n);
+    else run_gemm(gemm_nt_worker, x, w, y, r, kk, n);
+}
+
+/* Both traversals by name, for the test that they agree bit for bit. */
+void lo_matmul_order(int tiled, const float *x, size_t r, size_t kk, const float *w, size_t n, float *y) {
+    if (tiled) run_gemm_tiled(x, w, y, r, kk, n);
+    else run_gemm(gemm_nt_worker, x, w, y, r, kk, n);
 }
 
 /* matmul_t: x [r, kk] . w[n, kk]^T */
@@ -321,21 +436,16 @@ static void *attn_worker(void *arg) {
     return NULL;
 }
 
-/* Test infrastructure may set LAYA_ORACLE_THREADED_ATTENTION=1: the
- * (sequence, head) pairs are then split across LAYA_CPU_THREADS threads.
- * Every output element is computed by the same code either way, so the
- * results are identical; the timed CPU baseline keeps the reference's single
- * thread. */
-static int lo_threaded_attention(void) {
-    const char *v = getenv("LAYA_ORACLE_THREADED_ATTENTION");
-    return v && v[0] == '1';
-}
+/* With LAYA_ORACLE_FAST=1 (test infrastructure) the (sequence, head) pairs
+ * are split across LAYA_CPU_THREADS threads.  Every output element is
+ * computed by the same code either way, so the results are identical; the
+ * timed CPU baseline keeps the reference's single thread. */
 
 /* attention: q,k,v [n, nh, len, hd], mask [n, len, len] -> out [n*len, nh*hd] */
 void lo_attention(const float *q, const float *k, const float *v, const float *mask, size_t n,
                   size_t nh, size_t len, size_t hd, float *out) {
     const size_t pairs = n * nh;
-    size_t nt = lo_threaded_attention() ? (size_t)lo_nthreads() : 1;
+    size_t nt = lo_fast() ? (size_t)lo_nthreads() : 1;
     if (nt > pairs) nt = pairs ? pairs : 1;
     attn_job *jobs = (attn_job *)calloc(nt, sizeof(attn_job));
     pthread_t *tid = (pthread_t *)calloc(nt, sizeof(pthread_t));

@@ -90,6 +90,17 @@ def matmul(x, w):
     return y
 
 
+def matmul_order(x, w, tiled: bool):
+    """matmul with the reference's traversal or the register-tiled one that
+    LAYA_ORACLE_FAST selects, chosen explicitly."""
+    x, w = _f(x), _f(w)
+    r, kk = x.shape
+    assert w.shape[0] == kk, "matmul inner dim mismatch"
+    y = np.empty((r, w.shape[1]), np.float32)
+    lib().lo_matmul_order(ctypes.c_int(1 if tiled else 0), _p(x), _sz(r), _sz(kk), _p(w), _sz(w.shape[1]), _p(y))
+    return y
+
+
 def matmul_t(x, w):
     x, w = _f(x), _f(w)
     r, kk = x.shape

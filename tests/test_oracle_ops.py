@@ -115,8 +115,19 @@ def test_attention_mask_drops_keys():
     assert_close(out, [1.0, 0.0, 1.0 - p, p], 1e-5, "masked attention")
 
 
+@pytest.mark.parametrize("r,kk,n", [(1, 1, 1), (3, 5, 7), (4, 64, 8), (9, 33, 517), (40, 1024, 3072),
+                                    (66, 2624, 1024)])
+def test_tiled_matmul_is_bitwise_the_reference_traversal(r, kk, n):
+    """The register-tiled gemm_nt of LAYA_ORACLE_FAST performs the same
+    multiplies and adds in the same order per element as cpu/mod.rs:80-101."""
+    rng = np.random.default_rng(r * 7 + n)
+    x = rng.standard_normal((r, kk)).astype(np.float32)
+    w = rng.standard_normal((kk, n)).astype(np.float32)
+    assert O.matmul_order(x, w, tiled=False).tobytes() == O.matmul_order(x, w, tiled=True).tobytes()
+
+
 def test_threaded_attention_is_bitwise_the_single_threaded_one(monkeypatch):
-    """LAYA_ORACLE_THREADED_ATTENTION splits the (sequence, head) pairs over
+    """LAYA_ORACLE_FAST splits the attention's (sequence, head) pairs over
     threads; every output element runs the same code, so nothing changes."""
     rng = np.random.default_rng(5)
     n, nh, length, hd = 3, 4, 37, 8
@@ -126,7 +137,7 @@ def test_threaded_attention_is_bitwise_the_single_threaded_one(monkeypatch):
     mask = O.window_mask(att, n, length, 5)
     outs = []
     for flag in ("0", "1"):
-        monkeypatch.setenv("LAYA_ORACLE_THREADED_ATTENTION", flag)
+        monkeypatch.setenv("LAYA_ORACLE_FAST", flag)
         outs.append(O.attention(q, k, v, mask, nh, length))
     assert outs[0].tobytes() == outs[1].tobytes()
 
