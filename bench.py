@@ -847,6 +847,9 @@ def run_b200(args):
 
 def main():
     args = parse()
+    # the CPU baseline and the reference arm time the oracle with the
+    # reference's own traversal, never the test suite's faster one
+    os.environ.pop("LAYA_ORACLE_FAST", None)
     if args.impl == "reference":
         run_reference(args)
     else:
