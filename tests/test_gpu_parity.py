@@ -152,6 +152,36 @@ def test_single_layer_matches_the_oracle_layer(layer, lens, engine, oracle):
     assert rel < 1e-2, rel
 
 
+# Split-K edges (the engine cuts the residual GEMMs' K loop when their
+# 256 x 256 tiles fill at most half the clusters): 2304 rows is 9 row blocks,
+# 2 parts filling the part region to its last row; 2305 rows is 10 row blocks,
+# no split; 179 rows (one request) takes 4 parts.
+LENS_2304 = SPLIT_LENS[:-1] + [290]
+LENS_2305 = SPLIT_LENS[:-1] + [291]
+
+
+@pytest.mark.parametrize("layer,lens", [(1, LENS_2304), (3, LENS_2304), (1, LENS_2305), (1, [85, 94]),
+                                        (3, [85, 94])])
+def test_single_layer_at_the_split_k_edges(layer, lens, engine, oracle):
+    """One layer on an N(0,1) residual stream (configuration 1's input) at
+    the row counts where split-K starts, fills its part region or stops:
+    the engine's layer against the oracle's lo_encoder_layer."""
+    assert sum(LENS_2304) == 2304 and sum(LENS_2305) == 2305
+    req = synthetic_req(31, lens, 3, l=max(lens))
+    rng = np.random.default_rng(layer)
+    real = (req.att.reshape(req.n, req.l) != 0).ravel()
+    x = np.zeros((req.n * req.l, 1024), np.float32)
+    x[real] = rng.standard_normal((int(real.sum()), 1024)).astype(np.float32)
+    want = oracle.encoder_layer(req.n, req.l, req.att, layer, x).reshape(-1, 1024)[real]
+    p = engine.plan(req)
+    p.set_hidden(x[real])
+    p.run_layer(layer)
+    got = p.hidden()
+    p.close()
+    rel = np.abs(got - want).max() / np.abs(want).max()
+    assert rel < 1e-2, rel
+
+
 def test_single_layer_rejects_a_layer_out_of_range(engine):
     p = engine.plan(synthetic_req(12, [40], 2))
     for layer in (-1, 28):
