@@ -51,3 +51,23 @@ def test_null_arguments_are_rejected_with_a_status():
     assert lib.laya_plan_stats(None, None, None, None) == E.LAYA_E_INVALID
     assert "null" in lib.laya_last_error().decode()
     lib.laya_close(None)  # no-op
+
+
+def test_front_end_and_service_reject_bad_arguments_with_a_status():
+    """The front-end and HTTP-service entry points: null or out-of-range
+    arguments come back as LAYA_E_INVALID with a message, never an abort."""
+    from laya_rust_b200 import frontend as FE, serve as S
+    L = S.lib()
+    FE.lib()
+    out = ctypes.c_void_p()
+    n = ctypes.c_int64()
+    assert L.laya_serve_open(None, ctypes.byref(out)) == E.LAYA_E_INVALID
+    assert L.laya_serve_stop(None) == E.LAYA_E_INVALID
+    assert L.laya_serve_wait(None) == E.LAYA_E_INVALID
+    assert L.laya_serve_stats(None, None, 0) == E.LAYA_E_INVALID
+    L.laya_serve_close(None)  # no-op
+    assert L.laya_requests_merge(None, 2, ctypes.byref(out)) == E.LAYA_E_INVALID
+    assert L.laya_requests_merge(None, 0, None) == E.LAYA_E_INVALID
+    assert L.laya_requests_pack_windows(None, 16384, 4, ctypes.byref(n)) == E.LAYA_E_INVALID
+    assert L.laya_requests_pack(None, 16384, 0, ctypes.byref(n)) == E.LAYA_E_INVALID
+    assert E.lib().laya_last_error().decode()
