@@ -144,8 +144,13 @@ int laya_plan_hidden(laya_engine *e, laya_plan *p, float *x);
  * LAYA_E_INVALID.  No device memory is allocated by the call.  All calls share
  * that array: calls that overlap on the GPU race, so serialize them.  The
  * first call on a device (and with an engine) does set-up; make it before
- * any stream capture.  Enqueues on `stream` (a cudaStream_t, NULL for the
- * default stream) and returns after synchronizing it. */
+ * any stream capture.  Set-up belongs to the device's primary context: a call
+ * after the context was reset (cudaDeviceReset) finds the array's new address
+ * and redoes it.  The engine's weight pointers are looked up again after any
+ * weight upload.  The call runs on the engine's device and restores the
+ * caller's current device before it returns.  Enqueues on `stream` (a
+ * cudaStream_t, NULL for the default stream) and returns after synchronizing
+ * it. */
 #define LAYA_TAIL_STATIC_MAX_ROWS 2048
 int laya_decision_tail_static(laya_engine *e, const float *x, int n, int k, const int32_t *cls_row,
                               const int32_t *mk_row, const int8_t *mmask, float *logits, float *act,
@@ -167,9 +172,19 @@ int laya_selftest_gemm(int device, const uint16_t *a, const uint16_t *w, float *
  * *ms = mean device time per launch. */
 int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int epi, int flush_l2, int iters, float *ms);
 
+/* Test of the device-side bounded waits (failure detection without a GPU
+ * fault): arms the engine so that in its next forward
+ * (or plan run) the first launch of `kind` (0: the first GEMM, 1: the first
+ * attention launch) makes its TMA producers wait, before issuing any load, on
+ * an mbarrier that nothing ever completes, bounded by `limit_ns` (at most 2 s).
+ * The wait expires, the kernel records the error, unwinds and returns; the
+ * forward then reports LAYA_E_DEVICE_TIMEOUT and the engine stays usable.
+ * One-shot: the forward after that one runs normally. */
+int laya_test_timeout_next(laya_engine *e, int kind, uint64_t limit_ns);
+
 /* Ragged attention on qkv [R,3072] f16 (q,k pre-scaled) for sequences packed
  * back to back with lengths lens[n]; window < 0 for global.  out [R,1024] f32.
- * impl 1: the tcgen05 kernel the forward uses; impl 0: the mma.sync kernel. */
+ * impl must be 1 (the tcgen05 kernel the forward uses). */
 int laya_selftest_attention(int device, const uint16_t *qkv, const int32_t *lens, int n,
                             int window, float *out, int impl);
 

@@ -71,17 +71,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete.  Returns false (and
-// records `code` in *err) when the wall-clock limit passes or when *abort
-// (a shared-memory flag other roles raise on their own failure) is set.
+// records `code` in *err) when the wall-clock limit passes (limit_ns, or
+// kWaitLimitNs when 0) or when *abort (a shared-memory flag other roles
+// raise on their own failure) is set.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
-                                                  int code, volatile int* abort_flag) {
+                                                  int code, volatile int* abort_flag,
+                                                  unsigned long long limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long limit = limit_ns ? limit_ns : kWaitLimitNs;
   const unsigned long long t0 = global_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 63u) == 0) {
       if (abort_flag && *abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit) {
         atomicCAS(err, 0, code);
         if (abort_flag) *abort_flag = 1;
         return false;

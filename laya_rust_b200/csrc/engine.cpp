@@ -17,6 +17,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstdlib>
@@ -184,11 +185,10 @@ struct Weight {
 
 // Host-side plan of one request: validated and compacted (real tokens only).
 // Rows [row0, row0 + rows) of the compacted batch (whole sequences) whose
-// encoder and head layers run as one chain of launches; its attention blocks
-// are blocks[blk0, blk0 + nshort) (tiles of consecutive sequences of at most
-// kAttnTcQRows tokens) followed by nlong blocks of longer sequences.
+// encoder and head layers run as one chain of launches; its attention work
+// items are items[item0, item0 + nitems).
 struct RowGroup {
-  int row0 = 0, rows = 0, blk0 = 0, nshort = 0, nlong = 0;
+  int row0 = 0, rows = 0, item0 = 0, nitems = 0;
 };
 
 // With LAYA_ROW_GROUPS=2, batches of at least kSplitMinRows real tokens run as
@@ -238,12 +238,12 @@ int splitk_max() {
 }
 
 struct HostPlan {
-  int n = 0, l = 0, k = 0, R = 0, nblocks = 0;
-  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row, rowseq;
-  // attention work per row group: tiles (first row, rows) packing whole
-  // consecutive sequences of at most kAttnTcQRows tokens, then (sequence,
-  // first query row) blocks of longer ones, kAttnTcQRows apart
-  std::vector<int2> blocks;
+  int n = 0, l = 0, k = 0, R = 0, nitems = 0;
+  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row;
+  // (first row, end row) of each row's sequence
+  std::vector<int2> rowspan;
+  // attention work items per row group (see attention_items)
+  std::vector<int4> items;
   std::vector<RowGroup> groups;
   std::vector<uint8_t> rowtype;
   std::vector<int8_t> mmask;
@@ -251,7 +251,7 @@ struct HostPlan {
 
 // Offsets of each array inside one packed device buffer.
 struct PlanLayout {
-  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, blocks, rowtype, mmask, rowseq, total;
+  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, items, rowtype, mmask, rowspan, total;
 };
 
 size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -270,10 +270,10 @@ PlanLayout layout_for(const HostPlan& p) {
   L.seq_len = take(sizeof(int) * p.n);
   L.cls_row = take(sizeof(int) * p.n);
   L.mk_row = take(sizeof(int) * p.n * p.k);
-  L.blocks = take(sizeof(int2) * p.nblocks);
+  L.items = take(sizeof(int4) * p.nitems);
   L.rowtype = take(p.R);
   L.mmask = take((size_t)p.n * p.k);
-  L.rowseq = take(sizeof(int) * p.R);
+  L.rowspan = take(sizeof(int2) * p.R);
   L.total = o;
   return L;
 }
@@ -285,33 +285,49 @@ void pack(const HostPlan& p, const PlanLayout& L, uint8_t* dst) {
   memcpy(dst + L.seq_len, p.seq_len.data(), sizeof(int) * p.n);
   memcpy(dst + L.cls_row, p.cls_row.data(), sizeof(int) * p.n);
   memcpy(dst + L.mk_row, p.mk_row.data(), sizeof(int) * p.n * p.k);
-  memcpy(dst + L.blocks, p.blocks.data(), sizeof(int2) * p.nblocks);
+  memcpy(dst + L.items, p.items.data(), sizeof(int4) * p.nitems);
   memcpy(dst + L.rowtype, p.rowtype.data(), p.R);
   memcpy(dst + L.mmask, p.mmask.data(), (size_t)p.n * p.k);
-  memcpy(dst + L.rowseq, p.rowseq.data(), sizeof(int) * p.R);
+  memcpy(dst + L.rowspan, p.rowspan.data(), sizeof(int2) * p.R);
 }
 
-// Attention tiles for the sequences of at most kAttnTcQRows tokens among
-// [b0, b1): consecutive ones (adjacent in the compacted rows) share a tile
-// while their rows fit, as (first row, rows).
-void pack_short_tiles(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
-                      std::vector<int2>& out) {
+// Attention work items for the sequences [b0, b1): int4 (first query row,
+// query rows, sequence start row, sequence length).  First the 128-row
+// blocks of sequences longer than kAttnTcQRows, longest sequences first (they
+// see the most key blocks, so the persistent kernel's round-robin deals them
+// out first); then tiles packing consecutive shorter sequences (adjacent in
+// the compacted rows) while their rows fit in kAttnTcQRows, each tile one
+// item whose "sequence" is the tile itself (its rows still see only their
+// own sequence's keys, through the row spans).
+void attention_items(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
+                     std::vector<int4>& out) {
+  std::vector<int> longs;
+  for (int b = b0; b < b1; ++b)
+    if (len[b] > kAttnTcQRows) longs.push_back(b);
+  std::stable_sort(longs.begin(), longs.end(), [&](int x, int y) { return len[x] > len[y]; });
+  for (int b : longs)
+    for (int q0 = 0; q0 < len[b]; q0 += kAttnTcQRows)
+      out.push_back(make_int4(start[b] + q0, std::min(kAttnTcQRows, len[b] - q0), start[b], len[b]));
   int row0 = -1, rows = 0;
+  auto flush = [&] {
+    if (row0 >= 0) out.push_back(make_int4(row0, rows, row0, rows));
+    row0 = -1;
+    rows = 0;
+  };
   for (int b = b0; b < b1; ++b) {
     if (len[b] > kAttnTcQRows) {
-      if (row0 >= 0) out.push_back(make_int2(row0, rows));
-      row0 = -1;
+      flush();
       continue;
     }
     if (row0 >= 0 && start[b] == row0 + rows && rows + len[b] <= kAttnTcQRows) {
       rows += len[b];
     } else {
-      if (row0 >= 0) out.push_back(make_int2(row0, rows));
+      flush();
       row0 = start[b];
       rows = len[b];
     }
   }
-  if (row0 >= 0) out.push_back(make_int2(row0, rows));
+  flush();
 }
 
 // Validates a Req and compacts its real tokens.  The reference asserts
@@ -352,7 +368,7 @@ HostPlan make_plan(const laya_req* q) {
   p.tok.resize(R);
   p.pos.resize(R);
   p.rowtype.resize(R);
-  p.rowseq.resize(R);
+  p.rowspan.resize(R);
   for (int b = 0; b < p.n; ++b) {
     const int64_t* ids = q->ids + (size_t)b * p.l;
     for (int t = 0; t < p.l; ++t)
@@ -362,7 +378,7 @@ HostPlan make_plan(const laya_req* q) {
       p.tok[p.seq_start[b] + t] = (int)ids[t];
       p.pos[p.seq_start[b] + t] = t;
       p.rowtype[p.seq_start[b] + t] = (uint8_t)q->qtype[b];
-      p.rowseq[p.seq_start[b] + t] = b;
+      p.rowspan[p.seq_start[b] + t] = make_int2(p.seq_start[b], p.seq_start[b] + p.seq_len[b]);
     }
   }
   // two row groups of about R/2 rows, split at a sequence boundary
@@ -383,16 +399,12 @@ HostPlan make_plan(const laya_req* q) {
     const int b0 = bounds[gi], b1 = bounds[gi + 1];
     g.row0 = p.seq_start[b0];
     g.rows = (b1 < p.n ? p.seq_start[b1] : R) - g.row0;
-    g.blk0 = (int)p.blocks.size();
-    pack_short_tiles(p.seq_start, p.seq_len, b0, b1, p.blocks);
-    g.nshort = (int)p.blocks.size() - g.blk0;
-    for (int b = b0; b < b1; ++b)
-      if (p.seq_len[b] > kAttnTcQRows)
-        for (int q0 = 0; q0 < p.seq_len[b]; q0 += kAttnTcQRows) p.blocks.push_back(make_int2(b, q0));
-    g.nlong = (int)p.blocks.size() - g.blk0 - g.nshort;
+    g.item0 = (int)p.items.size();
+    attention_items(p.seq_start, p.seq_len, b0, b1, p.items);
+    g.nitems = (int)p.items.size() - g.item0;
     p.groups.push_back(g);
   }
-  p.nblocks = (int)p.blocks.size();
+  p.nitems = (int)p.items.size();
   p.cls_row.resize(p.n);
   p.mk_row.resize((size_t)p.n * p.k);
   p.mmask.resize((size_t)p.n * p.k);
@@ -469,7 +481,9 @@ struct Engine {
 
   // arena
   int cap_rows = 0, cap_mk = 0, cap_n = 0;
-  uint64_t arena_gen = 0;  // bumped on every reallocation; captured graphs record it
+  // bumped on every arena reallocation and weight upload; captured graphs and
+  // plan tensor maps record it
+  uint64_t arena_gen = 0;
   DevBuf x, t16, qkv, ctx, gate, hmlp, mk16, partial, out_logits, out_act, err, plan_buf;
   // split-K parts of the residual GEMMs, one region per row group, and the
   // parts each group's next LayerNorm still has to add
@@ -486,6 +500,13 @@ struct Engine {
   enum ProfKind { kProfQkv, kProfWo, kProfWi, kProfWo2, kProfHead, kProfAttn, kProfNorm, kProfTail };
   std::vector<cudaEvent_t>* prof_ev = nullptr;
   std::vector<int>* prof_kind = nullptr;
+
+  // The timeout test (laya_test_timeout_next): the next forward's first
+  // launch of the chosen kind waits on a barrier nothing completes, with
+  // this limit, so that its device-side wait expires and the kernel unwinds.
+  bool stuck_next = false;
+  int stuck_kind = 0;  // 0: the first GEMM, 1: the first attention launch
+  unsigned long long stuck_limit_ns = 0;
 
   // decision-tail weight pointers, looked up once (see tail_weights)
   TailWeights tail_cache{};
@@ -557,6 +578,11 @@ struct Engine {
     auto f32_at = [&](size_t i) {
       return is_f16 ? h2f_bits(static_cast<const uint16_t*>(data)[i]) : static_cast<const float*>(data)[i];
     };
+    // a weight that changes invalidates what holds its old device pointer:
+    // the cached decision-tail pointers and every captured forward graph
+    // (a plan's graph records the arena generation and is re-captured)
+    tail_cache_ready = false;
+    ++arena_gen;
     Weight& wt = w[name];
     switch (role.kind) {
       case Kind::Linear:
@@ -733,6 +759,12 @@ struct Engine {
     a.N = N;
     a.K = K;
     a.err = err.as<int>();
+    if (stuck_next && stuck_kind == 0) {
+      // the timeout test (see stuck_next)
+      a.stuck = 1;
+      a.wait_limit_ns = stuck_limit_ns;
+      stuck_next = false;
+    }
     // 256 x 128 tiles (twice the tiles per wave for N = 1024) measured slower
     // than 256 x 256 on the residual GEMMs: the smaller stages leave the TMA
     // latency exposed.  They stay available through launch_gemm's `bn`.
@@ -744,24 +776,28 @@ struct Engine {
     mark(kind);
   }
 
-  // Attention over the group's sequences: one launch for sequences of at most
-  // 128 tokens (single-pass kernel) and one for longer ones (two-pass kernel).
+  // Attention over the group's sequences: one launch of the flash kernel
+  // over the group's work items.
   void attention(const DevicePlan& dp, int gi, int window, cudaStream_t s, int64_t& nl) {
     const RowGroup& g = dp.host.groups[gi];
     const PlanLayout& L = dp.lay;
-    AttnArgs aa{qkv.as<__half>(), ctx.as<__half>(), dp.at<int>(L.seq_start), dp.at<int>(L.seq_len),
-                dp.at<int2>(L.blocks) + g.blk0, window, dp.at<int>(L.rowseq)};
-    if (g.nshort > 0) {
-      ck(launch_attention_tc(&dp.maps.qkv_tiles, aa, g.nshort, true, err.as<int>(), s), "attention");
-      ++nl;
-      mark(kProfAttn);
+    AttnArgs aa{};
+    aa.out = ctx.as<__half>();
+    aa.items = dp.at<int4>(L.items) + g.item0;
+    aa.rowspan = dp.at<int2>(L.rowspan);
+    aa.num_items = g.nitems;
+    aa.window = window;
+    aa.err = err.as<int>();
+    if (stuck_next && stuck_kind == 1) {
+      // the timeout test: this launch's producers wait on a barrier nothing
+      // completes, for stuck_limit_ns, then the kernel unwinds and reports
+      aa.stuck = 1;
+      aa.wait_limit_ns = stuck_limit_ns;
+      stuck_next = false;
     }
-    if (g.nlong > 0) {
-      aa.blocks += g.nshort;
-      ck(launch_attention_tc(&dp.maps.qkv_tiles, aa, g.nlong, false, err.as<int>(), s), "attention");
-      ++nl;
-      mark(kProfAttn);
-    }
+    ck(launch_attention_tc(&dp.maps.qkv_tiles, aa, num_sms, s), "attention");
+    ++nl;
+    mark(kProfAttn);
   }
 
   // LayerNorm of row group gi's residual rows into `out`; first adds the
@@ -1579,15 +1615,25 @@ int laya_bench_gemm(int device, int m, int n, int k, int tile_n, int epi, int fl
   });
 }
 
+int laya_test_timeout_next(laya_engine* e, int kind, uint64_t limit_ns) {
+  return guard([&] {
+    if (!e || (kind != 0 && kind != 1) || limit_ns == 0 || limit_ns > 2000000000ull)
+      throw Error(LAYA_E_INVALID, "test_timeout_next: kind must be 0 or 1 and 0 < limit_ns <= 2e9");
+    e->e->stuck_next = true;
+    e->e->stuck_kind = kind;
+    e->e->stuck_limit_ns = limit_ns;
+  });
+}
+
 int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens, int n, int window, float* out,
                             int impl) {
   return guard([&] {
-    if (!qkv || !lens || !out || n <= 0 || (impl != 0 && impl != 1))
-      throw Error(LAYA_E_INVALID, "selftest_attention: bad argument");
+    if (!qkv || !lens || !out || n <= 0 || impl != 1)
+      throw Error(LAYA_E_INVALID, "selftest_attention: bad argument (impl must be 1)");
     laya::ck(cudaSetDevice(device), "cudaSetDevice");
-    const int qrows = impl == 1 ? laya::kAttnTcQRows : laya::kAttnQRows;
+    int num_sms = 0;
+    laya::ck(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device), "device query");
     std::vector<int> start(n), len(n);
-    std::vector<int2> blocks;
     int R = 0;
     for (int b = 0; b < n; ++b) {
       if (lens[b] <= 0) throw Error(LAYA_E_INVALID, "selftest_attention: empty sequence");
@@ -1595,49 +1641,37 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
       len[b] = lens[b];
       R += lens[b];
     }
-    // tcgen05: tiles of consecutive short sequences first, then the long ones
-    int nshort = 0;
-    if (impl == 1) laya::pack_short_tiles(start, len, 0, n, blocks);
-    nshort = (int)blocks.size();
-    std::vector<int> rowseq(R);
+    std::vector<int4> items;
+    laya::attention_items(start, len, 0, n, items);
+    std::vector<int2> span(R);
     for (int b = 0; b < n; ++b)
-      for (int t = 0; t < len[b]; ++t) rowseq[start[b] + t] = b;
-    for (int b = 0; b < n; ++b)
-      if (impl == 0 || len[b] > qrows)
-        for (int q0 = 0; q0 < len[b]; q0 += qrows) blocks.push_back(make_int2(b, q0));
-    laya::DevBuf dq, dout, ds, dl, db, drs, derr;
+      for (int t = 0; t < len[b]; ++t) span[start[b] + t] = make_int2(start[b], start[b] + len[b]);
+    laya::DevBuf dq, dout, di, dsp, derr;
     dq.alloc((size_t)R * 3072 * 2, "qkv");
     dout.alloc((size_t)R * 1024 * 2, "out");
-    ds.alloc(n * 4, "start");
-    dl.alloc(n * 4, "len");
-    db.alloc(blocks.size() * sizeof(int2), "blocks");
-    drs.alloc((size_t)R * 4, "rowseq");
-    laya::ck(cudaMemcpy(drs.p, rowseq.data(), (size_t)R * 4, cudaMemcpyHostToDevice), "h2d");
+    di.alloc(items.size() * sizeof(int4), "items");
+    dsp.alloc((size_t)R * sizeof(int2), "rowspan");
     laya::ck(cudaMemcpy(dq.p, qkv, dq.bytes, cudaMemcpyHostToDevice), "h2d");
-    laya::ck(cudaMemcpy(ds.p, start.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
-    laya::ck(cudaMemcpy(dl.p, len.data(), n * 4, cudaMemcpyHostToDevice), "h2d");
-    laya::ck(cudaMemcpy(db.p, blocks.data(), blocks.size() * sizeof(int2), cudaMemcpyHostToDevice), "h2d");
-    laya::AttnArgs a{dq.as<__half>(), dout.as<__half>(), ds.as<int>(), dl.as<int>(), db.as<int2>(), window,
-                     drs.as<int>()};
-    if (impl == 1) {
-      derr.alloc(256, "err");
-      laya::ck(cudaMemset(derr.p, 0, 256), "memset");
-      CUtensorMap tm;
-      if (laya::make_tmap_2d(&tm, dq.p, false, R, 3072, 64, laya::kAttnTcQRows))
-        throw Error(LAYA_E_CUDA, "tensor map encode failed");
-      laya::ck(laya::launch_attention_tc(&tm, a, nshort, true, derr.as<int>(), 0), "attention launch");
-      laya::AttnArgs al = a;
-      al.blocks += nshort;
-      laya::ck(laya::launch_attention_tc(&tm, al, (int)blocks.size() - nshort, false, derr.as<int>(), 0),
-               "attention launch");
-      laya::ck(cudaDeviceSynchronize(), "attention run");
-      int ev = 0;
-      laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
-      if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("attention device wait expired (code %d)", ev));
-    } else {
-      laya::ck(laya::launch_attention(a, (int)blocks.size(), 0), "attention launch");
-      laya::ck(cudaDeviceSynchronize(), "attention run");
-    }
+    laya::ck(cudaMemcpy(di.p, items.data(), di.bytes, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(dsp.p, span.data(), dsp.bytes, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemset(dout.p, 0, dout.bytes), "memset");
+    derr.alloc(256, "err");
+    laya::ck(cudaMemset(derr.p, 0, 256), "memset");
+    CUtensorMap tm;
+    if (laya::make_tmap_2d(&tm, dq.p, false, R, 3072, 64, laya::kAttnTcQRows))
+      throw Error(LAYA_E_CUDA, "tensor map encode failed");
+    laya::AttnArgs a{};
+    a.out = dout.as<__half>();
+    a.items = di.as<int4>();
+    a.rowspan = dsp.as<int2>();
+    a.num_items = (int)items.size();
+    a.window = window;
+    a.err = derr.as<int>();
+    laya::ck(laya::launch_attention_tc(&tm, a, num_sms, 0), "attention launch");
+    laya::ck(cudaDeviceSynchronize(), "attention run");
+    int ev = 0;
+    laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");
+    if (ev) throw Error(LAYA_E_DEVICE_TIMEOUT, laya::fmt("attention device wait expired (code %d)", ev));
     std::vector<uint16_t> h((size_t)R * 1024);
     laya::ck(cudaMemcpy(h.data(), dout.p, h.size() * 2, cudaMemcpyDeviceToHost), "d2h");
     for (size_t i = 0; i < h.size(); ++i) out[i] = laya::h2f_bits(h[i]);

@@ -379,7 +379,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* tfull = empty + C::STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* stuck_bar = drain + 1;  // nothing ever arrives on it (the timeout test)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stuck_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -408,6 +409,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&tempty[i], 2 * EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(stuck_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -434,6 +436,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      if (args.stuck)
+        ok = mbar_wait_bounded(stuck_bar, 0, args.err, kErrGemmProducerWait, abort_flag, args.wait_limit_ns);
       // the A operand is read by the num_n clusters working on its row block
       // at about the same time, and not after: evict-first
       const uint64_t pol_a = l2_evict_first();
@@ -443,7 +447,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
         const int kb1 = (part + 1) * num_kb / S;
         for (int kb = part * num_kb / S; kb < kb1; ++kb) {
-          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag)) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag,
+                                 args.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -457,8 +462,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-      if (!ok) {
-        // give loads already in flight time to land before teardown
+      if (!ok || *abort_flag) {
+        // give loads already in flight time to land before teardown (also
+        // when another role of this CTA gave up while this loop completed)
         const unsigned long long t0 = global_ns();
         while (global_ns() - t0 < 2000000ull) __nanosleep(1000);
       }
@@ -474,14 +480,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         const int part = u % S;
         const int kb0 = part * num_kb / S, kb1 = (part + 1) * num_kb / S;
-        if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, args.err, kErrGemmMmaWait, abort_flag)) {
+        if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, args.err, kErrGemmMmaWait, abort_flag, args.wait_limit_ns)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait_bounded(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag)) {
+          if (!mbar_wait_bounded(&full[stage], phase, args.err, kErrGemmMmaWait, abort_flag, args.wait_limit_ns)) {
             ok = false;
             break;
           }
@@ -519,7 +525,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int tile = u / S, part = u - tile * S;
       int ok = 1;
       if (lane == 0)
-        ok = mbar_wait_bounded(&tfull[acc], aphase, args.err, kErrGemmEpilogueWait, abort_flag);
+        ok = mbar_wait_bounded(&tfull[acc], aphase, args.err, kErrGemmEpilogueWait, abort_flag, args.wait_limit_ns);
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) break;
       tc_fence_after();

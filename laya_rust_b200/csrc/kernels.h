@@ -56,6 +56,8 @@ struct GemmArgs {
   int n_valid;         // valid output columns for kEpiGeglu
   int splits;          // kEpiPartial: K parts (>= 1)
   int split_rows;      // kEpiPartial: output rows per part (multiple of 256, >= M)
+  unsigned long long wait_limit_ns;  // 0: the default bound (2 s)
+  int stuck;           // timeout test: the producers first wait on a barrier nothing completes
 };
 
 // Encodes a 2-D f16 K-major tensor map: rows x k elements, row stride k*2 B,
@@ -82,29 +84,27 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& maps, const GemmArgs& args
                         cudaStream_t stream, int bn = kGemmBN);
 
 // ---- attention over compacted sequences ----------------------------------------
-struct AttnArgs {
-  const __half* qkv;    // [R, 3072]
-  __half* out;          // [R, 1024]
-  const int* seq_start; // [n]
-  const int* seq_len;   // [n]
-  // [num_blocks]: for sequences of at most kAttnTcQRows tokens (the tcgen05
-  // single-pass launch) (first row, rows) of a tile of whole consecutive
-  // sequences packed back to back; otherwise (sequence, first query row)
-  const int2* blocks;
-  int window;           // < 0: global
-  const int* rowseq;    // [R] sequence of each row (packed tiles)
-};
-cudaError_t launch_attention(const AttnArgs& a, int num_blocks, cudaStream_t stream);
-constexpr int kAttnQRows = 64;
-// tcgen05 attention: blocks of kAttnTcQRows query rows; tm_qkv maps the qkv
-// buffer ([R, 3072] f16, box 64 columns x 128 rows, 128-byte swizzle).
-// short_seqs: the blocks are packed tiles of sequences of at most
-// kAttnTcQRows tokens (one key block, single pass, four CTAs per SM; each
-// query row sees only its own sequence's keys); otherwise the two-pass kernel
-// over (sequence, first query row) blocks.
+// Work items of 128 query rows (kAttnTcQRows): int4 (first query row, query
+// rows, first row of the sequence, sequence length).  A tile of whole
+// consecutive sequences of at most 128 tokens is one item with sequence
+// start = first row and length = rows (its rows see only their own
+// sequence, through rowspan); a longer sequence gives one item per 128-row
+// block.  Items whose queries see more key blocks come first.
 constexpr int kAttnTcQRows = 128;
-cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_blocks, bool short_seqs,
-                                int* err, cudaStream_t stream);
+struct AttnArgs {
+  __half* out;            // [R, 1024] context, token-major
+  const int4* items;      // [num_items]
+  const int2* rowspan;    // [R] (first row, end row) of each row's sequence
+  int num_items;
+  int window;             // < 0: global
+  int* err;               // device error word
+  unsigned long long wait_limit_ns;  // 0: the default bound (2 s)
+  int stuck;              // timeout test: the producer first waits on a barrier nothing completes
+};
+// tcgen05 flash attention (persistent, min(16 * items, num_sms) CTAs); tm_qkv
+// maps the qkv buffer ([R, 3072] f16, box 64 columns x 128 rows, 128-byte
+// swizzle): q at columns h*64, k at 1024 + h*64, v at 2048 + h*64.
+cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_sms, cudaStream_t stream);
 
 // ---- row kernels -----------------------------------------------------------------
 // x[r] = t[r] = LN(emb[tok[r]]) * w ; writes f32 residual and f16 copy

@@ -22,12 +22,16 @@
 //     call's contents; nothing in it needs to start at zero except the error
 //     word, which each call clears.  Calls whose work overlaps on the GPU
 //     (two streams, or two host threads) race on the array: serialize them;
-//   * the first call on a device looks up the array's device address with
-//     cudaGetSymbolAddress (host code cannot use the symbol itself: in host
-//     code it names a host-side shadow, not device memory) and encodes the
-//     TMA tensor map over it; the first call with a given engine caches that
-//     engine's weight pointers.  Make the first call before any stream
-//     capture.
+//   * every call looks up the array's device address with
+//     cudaGetSymbolAddress on the engine's device (host code cannot use the
+//     symbol itself: in host code it names a host-side shadow, not device
+//     memory).  The first call on a device, and any call after the address
+//     changed (a new primary context, e.g. after cudaDeviceReset), encodes the
+//     TMA tensor map over it.  The engine's weight pointers are cached until
+//     a weight is uploaded again.  Make the first call before any stream
+//     capture;
+//   * the call switches to the engine's device and restores the caller's
+//     current device before it returns.
 #include <mutex>
 
 #include "../../include/laya_b200.h"
@@ -59,22 +63,24 @@ struct DeviceState {
 DeviceState g_state[64];
 std::mutex g_mu;
 
-// Once per device, with that device current: resolve the array's device
-// address and build the tensor map the scorer GEMM reads it through.
+// With device `dev` current: resolve the array's device address and, when it
+// is new (first call on the device, or a new primary context since), build
+// the tensor map the scorer GEMM reads it through.
 int setup_device(int dev, DeviceState** out) {
   if (dev < 0 || dev >= 64) {
     set_last_error("decision_tail_static: device index out of range");
     return LAYA_E_INVALID;
   }
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_last_error(cudaGetErrorString(e));
+    return LAYA_E_CUDA;
+  }
   std::lock_guard<std::mutex> lock(g_mu);
   DeviceState& s = g_state[dev];
-  if (!s.ready) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_last_error(cudaGetErrorString(e));
-      return LAYA_E_CUDA;
-    }
+  if (!s.ready || s.base != p) {
+    s.ready = false;
     s.base = static_cast<unsigned char*>(p);
     if (make_tmap_f16(&s.rows_map, s.base, kStaticMaxRows, kHid, kGemmABoxRows) != 0) {
       set_last_error("decision_tail_static: tensor map encode failed");
@@ -85,6 +91,17 @@ int setup_device(int dev, DeviceState** out) {
   *out = &s;
   return LAYA_OK;
 }
+
+// Restores the caller's current device when the call returns.
+struct DeviceRestore {
+  int prev = -1;
+  DeviceRestore() {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+  }
+  ~DeviceRestore() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
 
 int fail(cudaError_t e) {
   set_last_error(cudaGetErrorString(e));
@@ -109,6 +126,7 @@ extern "C" int laya_decision_tail_static(laya_engine* e, const float* x, int n, 
   TailWeights w;
   int status = LAYA_OK;
   if (!engine_tail_weights(e, &w, &status)) return status;
+  DeviceRestore restore;
   cudaError_t ce = cudaSetDevice(w.device);
   if (ce != cudaSuccess) return fail(ce);
   DeviceState* s = nullptr;

@@ -77,6 +77,7 @@ def lib():
         L.laya_stream.argtypes = [vp]
         L.laya_stream.restype = vp
         L.laya_decision_tail_static.argtypes = [vp, vp, ctypes.c_int, ctypes.c_int, vp, vp, vp, vp, vp, vp]
+        L.laya_test_timeout_next.argtypes = [vp, ctypes.c_int, ctypes.c_uint64]
         L.laya_selftest_gemm.argtypes = [ctypes.c_int, vp, vp, _f32p, ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_int]
         L.laya_selftest_attention.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_int32),
@@ -257,6 +258,12 @@ class Engine:
         _check(lib().laya_decision_tail_static(self._h, x, n, k, cls_row, mk_row, mmask, logits, act,
                                                stream or None))
 
+    def test_timeout_next(self, kind: int, limit_ns: int = 1_000_000) -> None:
+        """Arms the next forward's first GEMM (kind 0) or attention launch
+        (kind 1) to wait on a barrier nothing completes, bounded by limit_ns;
+        that forward then raises LayaError(LAYA_E_DEVICE_TIMEOUT)."""
+        _check(lib().laya_test_timeout_next(self._h, kind, limit_ns))
+
     def stream(self) -> int:
         return lib().laya_stream(self._h) or 0
 
@@ -284,7 +291,7 @@ def selftest_gemm(a: np.ndarray, w: np.ndarray, device: int = 0, tile_n: int = 2
 
 def selftest_attention(qkv: np.ndarray, lens, window: int, device: int = 0, impl: int = 1) -> np.ndarray:
     """Ragged attention on packed qkv [R, 3072] f16; returns [R, 1024] f32.
-    impl 1: the tcgen05 kernel the forward uses; impl 0: the mma.sync kernel."""
+    impl 1: the tcgen05 kernel the forward uses (the only one)."""
     qkv = np.ascontiguousarray(qkv, dtype=np.float16)
     lens = np.ascontiguousarray(lens, dtype=np.int32)
     out = np.empty((qkv.shape[0], 1024), np.float32)

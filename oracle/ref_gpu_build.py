@@ -11,6 +11,9 @@ together with the C++ restatement of the host schedule
 (oracle/ref_gpu_schedule.cu), linked to cuBLAS for the reference's FP32
 SGEMMs.  Without the reference tree (the GPU box) it keeps an existing build.
 
+The reference tree is given as an argument or by LAYA_REFERENCE_ROOT; with
+neither, an existing build is kept and nothing is compiled.
+
 Usage: python oracle/ref_gpu_build.py [reference-root]
 """
 import os
@@ -23,9 +26,10 @@ LIB = os.path.join(OUT, "libref_gpu.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
-def build(ref_root: str = "/root/reference", force: bool = False) -> str | None:
-    src = os.path.join(ref_root, "src", "backend", "cuda", "kernels.rs")
-    if not os.path.exists(src):
+def build(ref_root: str | None = None, force: bool = False) -> str | None:
+    ref_root = ref_root or os.environ.get("LAYA_REFERENCE_ROOT")
+    src = os.path.join(ref_root, "src", "backend", "cuda", "kernels.rs") if ref_root else ""
+    if not src or not os.path.exists(src):
         return LIB if os.path.exists(LIB) else None
     text = open(src).read()
     a = text.index('r#"') + 3
@@ -47,4 +51,5 @@ def build(ref_root: str = "/root/reference", force: bool = False) -> str | None:
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", force="--force" in sys.argv))
+    args = [a for a in sys.argv[1:] if a != "--force"]
+    print(build(args[0] if args else None, force="--force" in sys.argv))

@@ -61,4 +61,7 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LAYA_REFERENCE_ROOT")
+    if not root:
+        sys.exit("usage: make_fixture_requests.py REFERENCE_ROOT (or set LAYA_REFERENCE_ROOT)")
+    main(root)

@@ -2,7 +2,7 @@
 scores -> response JSON, against the reference's run_all restated on the CPU
 (oracle/frontend_ref.py around the C oracle's forward), for the reference's
 fixture requests and a few synthetic ones.  Answers must agree: the same
-questions in the same order, the same choices, probabilities within 2e-2
+questions in the same order, the same choices (strictly), probabilities within 2e-2
 (the logits' tolerance, through a softmax), identical usage."""
 import json
 import os
@@ -59,11 +59,11 @@ def close_answers(got, want, name, ordered=True):
         g, w = got[qid], want[qid]
         assert g["type"] == w["type"] and set(g) == set(w), (name, qid)
         if "choice" in w:
-            pw = np.array(list(w["probabilities"].values()))
-            # the same choice unless the top two are within the tolerance
-            top = np.sort(pw)[-2:]
-            if top[1] - top[0] > 4e-2:
-                assert g["choice"] == w["choice"], (name, qid)
+            # always the same choice; a disagreement reports the reference's
+            # top-2 probability margin
+            pw = np.sort(np.array(list(w["probabilities"].values())))
+            margin = float(pw[-1] - pw[-2]) if len(pw) > 1 else float("inf")
+            assert g["choice"] == w["choice"], (name, qid, "reference top-2 margin", margin)
         for key in ("probabilities",):
             if key in w:
                 for k in w[key]:

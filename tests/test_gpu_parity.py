@@ -17,12 +17,12 @@ import pytest
 from laya_rust_b200 import arch, modelgen
 from laya_rust_b200 import engine as E
 from laya_rust_b200.engine import Req
+from _parity import compare as shared_compare
 
 pytestmark = pytest.mark.gpu
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 FIXTURES = json.load(open(os.path.join(HERE, "golden", "fixture_requests.json")))
-ATOL, RTOL = 2e-2, 1e-2
 
 
 @pytest.fixture(scope="module")
@@ -90,20 +90,8 @@ CASES = fixture_reqs() + [
 
 
 def compare(req, got, want_logits, want_act):
-    mm = req.mmask.reshape(req.n, req.k) != 0
-    gl = got.logits.reshape(req.n, req.k)
-    wl = want_logits.reshape(req.n, req.k)
-    assert np.all(gl[~mm] == -10000.0) and np.all(wl[~mm] == -10000.0)
-    for name, g, w in (("logits", gl[mm], wl[mm]), ("act", got.act, want_act)):
-        err = np.abs(g - w)
-        assert np.all(np.isfinite(g)), name
-        assert err.max() <= ATOL, (name, float(err.max()))
-        assert np.all(err <= ATOL + RTOL * np.abs(w)), (name, float((err - RTOL * np.abs(w)).max()))
-    for b in range(req.n):
-        v = np.flatnonzero(mm[b])
-        if len(v) > 1:
-            assert np.argmax(gl[b, v]) == np.argmax(wl[b, v]), (b, gl[b, v], wl[b, v])
-    return float(np.abs(gl[mm] - wl[mm]).max()), float(np.abs(got.act - want_act).max())
+    el, ea, _ = shared_compare(req.n, req.k, req.mmask, got.logits, got.act, want_logits, want_act)
+    return el, ea
 
 
 @pytest.mark.parametrize("name,req", CASES, ids=[c[0] for c in CASES])

@@ -81,3 +81,24 @@ def test_static_tail_rejects_more_rows_than_its_array_holds(engine):
         engine.decision_tail_static(x.data_ptr(), 1, 4096, idx.data_ptr(), idx.data_ptr(), mm.data_ptr(),
                                     out.data_ptr(), out.data_ptr())
     assert ei.value.code == E.LAYA_E_INVALID
+
+
+def test_static_tail_follows_a_weight_uploaded_again():
+    """A weight uploaded after the first call (here the scorer's output bias)
+    must reach the static tail too: it caches the engine's weight pointers and
+    drops them on any upload.  Own engine, so the shared one keeps its weights."""
+    eng = E.Engine(modelgen.cached_model(seed=0), device=0)
+    try:
+        req = workloads.forward_16k(seed=7)
+        taps = {}
+        eng.forward(req, taps=taps)
+        inputs = compacted_inputs(req, taps)
+        run_static(eng, req, inputs)                       # caches the pointers
+        eng.upload_f32("scorer.3.bias", np.array([0.25], np.float32))
+        out = eng.forward(req)
+        got = run_static(eng, req, inputs)
+        check(got, (out.logits, out.act))
+        mm = req.mmask != 0
+        assert np.all(got[0][~mm] == -10000.0)
+    finally:
+        eng.close()
