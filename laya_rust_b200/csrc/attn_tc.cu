@@ -116,6 +116,16 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// Bits j of a 32-key chunk with a <= j < b (a, b relative to the chunk, any
+// integers): the keys of the chunk one query row can see.
+__device__ __forceinline__ uint32_t chunk_mask(int a, int b) {
+  const int lo = a < 0 ? 0 : (a > 32 ? 32 : a);
+  const int hi = b < 0 ? 0 : (b > 32 ? 32 : b);
+  if (hi <= lo) return 0u;
+  const uint64_t m = ((1ull << hi) - 1ull) & ~((1ull << lo) - 1ull);
+  return static_cast<uint32_t>(m);
+}
+
 // The key blocks a unit's queries can see: [kb0, kb1) of 128 keys counted
 // from the sequence's first row (windowed on local layers).
 struct ItemGeom {
@@ -380,34 +390,28 @@ __global__ void __launch_bounds__(THREADS, 1)
           break;
         }
         tc_fence_after();
-        uint32_t sv[TK];
-        {
-          uint32_t (&c0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-          uint32_t (&c1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-          uint32_t (&c2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[64]);
-          uint32_t (&c3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[96]);
-          tmem_ld_32x32b_x32(t_s, c0);
-          tmem_ld_32x32b_x32(t_s + 32, c1);
-          tmem_ld_32x32b_x32(t_s + 64, c2);
-          tmem_ld_32x32b_x32(t_s + 96, c3);
-          tmem_ld_wait();
-        }
+        // keys [a, b) of this block are visible to the row (block-relative)
         const int kbase = g.k_row0 + jj * TK;
-        // block maximum over the visible keys
-        float mb = -INFINITY;
-#pragma unroll
+        const int a0 = lo - kbase, b0 = hi - kbase;
+        // pass 1: block maximum, streaming S from TMEM 32 keys at a time;
+        // a chunk no row of the warp can see is skipped (warp-uniformly)
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
-          const int k0 = kbase + 32 * ch;
-          if (k0 + 32 <= lo || k0 >= hi) continue;
-          if (k0 >= lo && k0 + 32 <= hi) {
+          const uint32_t mask = chunk_mask(a0 - 32 * ch, b0 - 32 * ch);
+          if (!__any_sync(0xffffffffu, mask != 0u)) continue;
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_s + 32 * ch, v);
+          tmem_ld_wait();
+          if (__all_sync(0xffffffffu, mask == 0xffffffffu)) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) mb = fmaxf(mb, u2f(sv[32 * ch + j]));
+            for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], u2f(v[j]));
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (k0 + j >= lo && k0 + j < hi) mb = fmaxf(mb, u2f(sv[32 * ch + j]));
+            for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], (mask >> j) & 1u ? u2f(v[j]) : -INFINITY);
           }
         }
+        const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
         const float m_new = fmaxf(m_run, mb);
         const float m_use = m_new == -INFINITY ? 0.0f : m_new;
         const float ms = m_use * L2E;
@@ -424,33 +428,35 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           tc_fence_after();
         }
-        float sum = 0.0f;
-#pragma unroll
+        // pass 2: P = 2^(s log2e - max) (0 where hidden) as f16 into this
+        // row of P (chunk ch -> K atom ch / 2, 16-byte chunks 4 (ch % 2) ..)
+        float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 1
         for (int ch = 0; ch < 4; ++ch) {
-          const int k0 = kbase + 32 * ch;
+          const uint32_t mask = chunk_mask(a0 - 32 * ch, b0 - 32 * ch);
           uint32_t w[16];
-          if (k0 + 32 <= lo || k0 >= hi) {
+          if (!__any_sync(0xffffffffu, mask != 0u)) {
 #pragma unroll
             for (int j = 0; j < 16; ++j) w[j] = 0u;
-          } else if (k0 >= lo && k0 + 32 <= hi) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const float p0 = fast_exp2(fmaf(u2f(sv[32 * ch + j]), L2E, -ms));
-              const float p1 = fast_exp2(fmaf(u2f(sv[32 * ch + j + 1]), L2E, -ms));
-              sum += p0 + p1;
-              w[j / 2] = pack_half2(p0, p1);
-            }
           } else {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_s + 32 * ch, v);
+            tmem_ld_wait();
+            float p[32];
+            if (__all_sync(0xffffffffu, mask == 0xffffffffu)) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) p[j] = fast_exp2(fmaf(u2f(v[j]), L2E, -ms));
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                p[j] = fast_exp2((mask >> j) & 1u ? fmaf(u2f(v[j]), L2E, -ms) : -INFINITY);
+            }
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
-              const bool v0 = k0 + j >= lo && k0 + j < hi, v1 = k0 + j + 1 >= lo && k0 + j + 1 < hi;
-              const float p0 = v0 ? fast_exp2(fmaf(u2f(sv[32 * ch + j]), L2E, -ms)) : 0.0f;
-              const float p1 = v1 ? fast_exp2(fmaf(u2f(sv[32 * ch + j + 1]), L2E, -ms)) : 0.0f;
-              sum += p0 + p1;
-              w[j / 2] = pack_half2(p0, p1);
+              sm[(j >> 1) & 3] += p[j] + p[j + 1];
+              w[j / 2] = pack_half2(p[j], p[j + 1]);
             }
           }
-          // chunk ch -> K atom ch / 2, 16-byte chunks 4 * (ch % 2) .. of this row
           uint8_t* pr = prow + (ch >> 1) * TILE_BYTES;
           const int c0 = (ch & 1) * 4;
 #pragma unroll
@@ -458,8 +464,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             *reinterpret_cast<uint4*>(pr + (((c0 + x) ^ (row & 7)) << 4)) =
                 make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
         }
+        const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
         l_run = jj == 0 ? sum : l_run * alpha + sum;
-        if (jj > 0 && alpha != 1.0f) {
+        // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp
+        // rescales when any of its rows' maximum grew (alpha is 1 elsewhere)
+        if (jj > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
           uint32_t o[32];
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
