@@ -551,8 +551,10 @@ def fixture_parity(config, req, out):
 
 def layer_launches(req):
     """Kernels laya_plan_run_layer enqueues: two row norms, four GEMMs and one
-    attention launch (one flash kernel over every work item of the batch)."""
-    return 7
+    attention launch per kind of sequence present (at most 128 tokens: the
+    single-pass kernel over packed tiles; longer: the flash kernel)."""
+    lens = (req.att.reshape(req.n, req.l) != 0).sum(1)
+    return 6 + int((lens <= 128).any()) + int((lens > 128).any())
 
 
 def layer_flops(req, global_layer):

@@ -18,7 +18,7 @@ LIB_DIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIB_DIR, "liblaya_b200.so")
 OBJ_DIR = os.path.join(ROOT, "_build", "obj")
 
-SOURCES = ["gemm.cu", "attn_tc.cu", "rownorm.cu", "tail.cu", "tail_static.cu", "engine.cpp",
+SOURCES = ["gemm.cu", "attn_tc.cu", "attn_short.cu", "rownorm.cu", "tail.cu", "tail_static.cu", "engine.cpp",
            "gguf_reader.cpp", "json.cpp", "frontend.cpp", "serve.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "gguf_reader.h", "json.h", "unicode_tables.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")

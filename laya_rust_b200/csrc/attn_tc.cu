@@ -6,42 +6,56 @@
 // already scaled; a key is visible to a query when it is a real token of
 // the same sequence and, on local layers, within +-window positions.  No
 // mask tensor exists: each query row derives its visible key interval
-// [lo, hi) from its sequence's row span and the window.
+// [lo, hi) from its sequence and the window.
 //
-// Work: a unit is (item, head); an item is 128 query rows of the compacted
-// batch with the key blocks they can see.  Items are either a tile of whole
-// consecutive sequences of at most 128 tokens (one key block: the tile
-// itself) or a 128-row block of a longer sequence (1-4 key blocks of 128,
-// those outside the window skipped).  One CTA per SM walks the units
+// Work: a unit is (item, head); an item is a block of at most 128 query
+// rows of one sequence (one per 128 rows) with the key blocks of 128 they
+// can see (1-4; blocks outside the window skipped).  Only a sequence's own
+// rows are loaded, in 32-row TMA boxes.  One CTA per SM walks the units
 // blockIdx.x, blockIdx.x + gridDim.x, ...; unit k of a CTA goes to slot
 // k & 1, so two units are in flight per CTA and one slot's softmax overlaps
 // the other slot's MMAs and loads.
 //
-// Roles (320 threads):
-//   warp 0      TMA producer: Q of each unit into the slot's Q buffer, then
-//               its K and V blocks into a 3-stage ring (32 KB per stage)
-//   warp 1      TMEM allocation; one thread issues the MMAs:
-//                 S[slot] = Q . K_j^T        (M=128, N=128, K=64) -> TMEM
-//                 O[slot] += P_j . V_j       (M=128, N=64,  K=128) -> TMEM
-//               in a fixed order shared with the producer (the two slots'
-//               key-block steps alternate; each S is followed by the P.V of
-//               the step before it)
-//   warps 2-5   softmax warpgroup of slot 0, warps 6-9 of slot 1: thread t
-//               owns query row t = TMEM lane t.  Per key block it reads its
-//               128 scores, takes the running maximum, writes
-//               P = exp(s - max) as f16 into the slot's P buffer (the
-//               swizzled K-major operand layout), rescales its O row in TMEM
-//               when the maximum grew, and accumulates the row sum; after
-//               the unit's last block it scales O by 1 / sum and stores the
-//               row's 64 f16 values.
-// Shared memory: Q 2 x 16 KB, K/V ring 3 x 32 KB, P 2 x 32 KB (193 KB).
-// TMEM: S 2 x 128 columns, O 2 x 64 columns (512 allocated).
+// Roles (608 threads):
+//   warp 0      TMA producer of Q (one buffer per slot) and K blocks (a
+//               3-stage ring, a stage freed once its S is computed)
+//   warp 1      TMA producer of V blocks (a 3-stage ring, a stage freed once
+//               its P.V is done): K loads run ahead of the P.V they wait on
+//   warp 2      TMEM allocation; one thread issues the MMAs:
+//                 S[slot] = Q . K_j^T          (M=128, N=128, K=64)
+//                 O[slot] += P_j . [V_j | 1]   (M=128, N=80,  K=128)
+//               The B operand of the second is V (64 columns) followed by an
+//               all-ones block, so O's column 64 accumulates the row sums of
+//               P in f32 (the sums of exactly the f16 values multiplied
+//               into V).  Both run in a fixed step order shared with the
+//               producers (the two slots' key-block steps alternate; each S
+//               is followed by the P.V of the step before it).
+//   warps 3-18  softmax, four warpgroups: (slot, half) = (0,0) (0,1) (1,0)
+//               (1,1).  Thread t of a warpgroup owns query row t = TMEM lane
+//               t and, of each key block, the 64 keys of its half.  Per key
+//               block it reads its scores from TMEM in 32-key chunks (chunks
+//               no row of the warp can see are skipped; chunks every row of
+//               the warp sees fully take a path without selects), takes its
+//               half's maximum, exchanges it with the other half's thread of
+//               the same row through shared memory (a 64-thread named
+//               barrier per slot and lane quarter), writes
+//               P = 2^(s log2 e - max) with the packed f16 exponential into
+//               its half of the row of P (the swizzled K-major operand
+//               layout, one 64-key atom per half) and rescales its columns of
+//               the row's O (and the sum column) in TMEM when the maximum
+//               grew.  After the unit's last block each half scales its 32
+//               of the row's 64 outputs by 1 / sum and stores them.
+// Shared memory: Q 2 x 16 KB, K 3 x 16 KB, V 3 x 16 KB, ones 16 KB, P 2 x 32
+// KB, the CTA's first 64 work items, the max exchange (about 212 KB).
+// TMEM: S 2 x 128 columns, O 2 x 80 columns (at 256 and 384; 512 allocated).
 //
 // Every wait is bounded (2 s by default).  On expiry the waiting thread
-// records an error code and raises the CTA's abort flag; every role leaves
-// its loop at its next wait, the MMA thread waits (bounded) for the MMAs it
-// issued, the CTA lingers 2 ms so TMA loads in flight land, and TMEM is
-// freed.  The host reads the error word after the forward.
+// records an error code and raises the CTA's abort flag; every role stops
+// waiting and working (the softmax warps still pass their named barriers,
+// the same number as their partners, so none is left waiting), the MMA
+// thread waits (bounded) for the MMAs it issued, the CTA lingers 2 ms so
+// TMA loads in flight land, and TMEM is freed.  The host reads the error
+// word after the forward.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -52,36 +66,48 @@ namespace {
 constexpr int TQ = 128;                  // query rows per item
 constexpr int TK = 128;                  // keys per block
 constexpr int D = 64;                    // head dim
-constexpr int NKV = 3;                   // K/V ring stages
-constexpr int THREADS = 320;
+constexpr int DO = 80;                   // O columns: 64 outputs + the sum block
+constexpr int BOX = 32;                  // rows per TMA box
+constexpr int NK = 3;                    // K ring stages
+constexpr int NV = 3;                    // V ring stages
+constexpr int CTRL_WARPS = 3;            // Q/K producer, V producer, MMA
+constexpr int SOFTMAX_WARPS = 16;
+constexpr int THREADS = 32 * (CTRL_WARPS + SOFTMAX_WARPS);
 constexpr int TILE_BYTES = TQ * D * 2;   // 16 KB: one [128 x 64] f16 tile
-constexpr int KV_BYTES = 2 * TILE_BYTES; // K then V
+constexpr int BOX_BYTES = BOX * D * 2;   // 4 KB
 constexpr int P_BYTES = 2 * TILE_BYTES;  // P [128 x 128] f16: two 64-key atoms
+constexpr int MAX_UNITS = 64;            // work items cached in shared memory
 constexpr int OFF_Q = 0;
-constexpr int OFF_KV = OFF_Q + 2 * TILE_BYTES;
-constexpr int OFF_P = OFF_KV + NKV * KV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-// barriers: q_full[2] q_empty[2] kv_full[NKV] kv_empty[NKV] s_full[2]
-// p_full[2] pv_done[2] drain stuck, then the TMEM address and the abort flag
-constexpr int NBARS = 2 + 2 + NKV + NKV + 2 + 2 + 2 + 2;
+constexpr int OFF_K = OFF_Q + 2 * TILE_BYTES;
+constexpr int OFF_V = OFF_K + NK * TILE_BYTES;
+constexpr int OFF_ONES = OFF_V + NV * TILE_BYTES;             // after every V stage (positive LBO)
+constexpr int OFF_P = OFF_ONES + TILE_BYTES;
+constexpr int OFF_ITEMS = OFF_P + 2 * P_BYTES;                 // int4[MAX_UNITS]
+constexpr int OFF_XMAX = OFF_ITEMS + MAX_UNITS * 16;           // f32[slot][parity][half][128]
+constexpr int OFF_BAR = OFF_XMAX + 2 * 2 * 2 * TQ * 4;
+// barriers: q_full[2] q_empty[2] k_full[NK] k_empty[NK] v_full[NV]
+// v_empty[NV] s_full[2] p_full[2] pv_done[2] drain stuck, then the TMEM
+// address and the abort flag
+constexpr int NBARS = 2 + 2 + 2 * NK + 2 * NV + 2 + 2 + 2 + 2;
 constexpr size_t SMEM = 1024 + OFF_BAR + NBARS * 8 + 16;
 constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0;                 // S[slot] at slot * 128
-constexpr int O_COL = 256;               // O[slot] at 256 + slot * 64
+constexpr int O_COL = 256;               // O[slot] at 256 + slot * 128 (80 used)
 constexpr float L2E = 1.4426950408889634f;
 
 // S: A = Q (K-major), B = K block (K-major), M = 128, N = 128
 constexpr uint32_t IDESC_QK = umma_idesc_f16(TQ, TK);
-// O: A = P (K-major over keys), B = V (MN-major: d contiguous), M = 128, N = 64
-constexpr uint32_t IDESC_PV = umma_idesc_f16(TQ, D) | (1u << 16);
+// O: A = P (K-major over keys), B = [V | ones] (MN-major), M = 128, N = 80
+constexpr uint32_t IDESC_PV = umma_idesc_f16(TQ, DO) | (1u << 16);
 
-// Descriptor of an MN-major operand tile written by TMA with 128-byte
-// swizzle: rows are K (keys), 128 B of N (64 f16) per row; 8-row groups
-// 1024 B apart (stride byte offset); a single 64-wide N block.
-__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr) {
+// Descriptor of an MN-major operand written with 128-byte swizzle: rows are
+// K (keys), 128 B of N (64 f16) per row, 8-row groups 1024 B apart (stride
+// byte offset); the next 64 N columns start `lbo` bytes further (leading
+// byte offset): here the all-ones block.
+__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t smem_addr, uint32_t lbo) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>(TILE_BYTES >> 4) << 16;  // next N block (unused: N = 64)
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>(1024u >> 4) << 32;
   d |= static_cast<uint64_t>(1u) << 46;
   d |= static_cast<uint64_t>(2u) << 61;
@@ -102,6 +128,15 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// (2^x0, 2^x1) as packed f16 (x0 in the low half): the arguments are
+// rounded to f16 and one MUFU op exponentiates both.
+__device__ __forceinline__ uint32_t exp2_h2(float x0, float x1) {
+  uint32_t h, r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(x1), "f"(x0));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(h));
+  return r;
+}
+
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
@@ -114,7 +149,22 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// One 32-bit column of 32 lanes (the row sum).
+__device__ __forceinline__ uint32_t tmem_ld_32x32b_x1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];" : "=r"(r) : "r"(taddr));
+  return r;
+}
+__device__ __forceinline__ void tmem_st_32x32b_x1(uint32_t taddr, uint32_t v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};" ::"r"(taddr), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Barrier `id` (1..8) over the `count` threads of two warps.
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 // Bits j of a 32-key chunk with a <= j < b (a, b relative to the chunk, any
 // integers): the keys of the chunk one query row can see.
@@ -126,15 +176,15 @@ __device__ __forceinline__ uint32_t chunk_mask(int a, int b) {
   return static_cast<uint32_t>(m);
 }
 
-// The key blocks a unit's queries can see: [kb0, kb1) of 128 keys counted
-// from the sequence's first row (windowed on local layers).
+// A unit's item: query rows [q_row0, q_row0 + q_rows) of the sequence
+// [seq0, seq1), and the key blocks [k_row0 + 128 j, ...), j < nkb, they can
+// see (windowed on local layers).
 struct ItemGeom {
-  int q_row0, q_rows, k_row0, nkb;
+  int q_row0, q_rows, k_row0, nkb, seq1;
 };
 
 __device__ __forceinline__ ItemGeom item_geom(const int4 it, int window) {
-  // it = (first query row, query rows, sequence start row, sequence length);
-  // a tile of packed short sequences has start = first row, length = rows
+  // it = (first query row, query rows, sequence start row, sequence length)
   const int q0 = it.x - it.z, len = it.w;
   int lo = 0, hi = len;
   if (window >= 0) {
@@ -142,45 +192,59 @@ __device__ __forceinline__ ItemGeom item_geom(const int4 it, int window) {
     hi = q0 + it.y + window < len ? q0 + it.y + window : len;
   }
   const int kb0 = lo / TK, kb1 = (hi + TK - 1) / TK;
-  return ItemGeom{it.x, it.y, it.z + kb0 * TK, kb1 - kb0};
+  return ItemGeom{it.x, it.y, it.z + kb0 * TK, kb1 - kb0 > 0 ? kb1 - kb0 : 1, it.z + len};
 }
 
-// The fixed order of key-block steps shared by the producer and the MMA
+// 32-row boxes a tile of rows [r0, min(r0 + 128, end)) needs (at least one).
+__device__ __forceinline__ int boxes(int r0, int end) {
+  const int n = end - r0 < TQ ? end - r0 : TQ;
+  return n <= 0 ? 1 : (n + BOX - 1) / BOX;
+}
+
+// The work item of this CTA's unit k (from the shared-memory cache when it
+// holds it).
+__device__ __forceinline__ int4 unit_item(const AttnArgs& a, const int4* cache, int k) {
+  if (k < MAX_UNITS) return cache[k];
+  return __ldg(a.items + ((blockIdx.x + k * gridDim.x) >> 4));
+}
+
+// The fixed order of key-block steps shared by the producers and the MMA
 // thread: the two slots' steps alternate (a slot whose units are exhausted
 // drops out).  Slot s holds this CTA's units k = s, s + 2, ...
 struct StepIter {
-  const AttnArgs* a;
-  int units;                 // units of this CTA
-  int k[2], j[2], nkb[2], n[2];
+  int units;
+  int k0, k1, j0, j1, nkb0, nkb1, n0, n1;
   int turn;
-  __device__ __forceinline__ void load(int s) {
-    if (k[s] < units) {
-      const int u = blockIdx.x + k[s] * gridDim.x;
-      nkb[s] = item_geom(a->items[u >> 4], a->window).nkb;
-      if (nkb[s] <= 0) nkb[s] = 1;  // never: every item has a key block
-    }
-  }
-  __device__ __forceinline__ void init(const AttnArgs* args, int cta_units) {
-    a = args;
+  __device__ __forceinline__ void init(const AttnArgs& a, const int4* cache, int cta_units) {
     units = cta_units;
-    k[0] = 0; k[1] = 1; j[0] = j[1] = 0; n[0] = n[1] = 0; turn = 0;
-    load(0);
-    load(1);
+    k0 = 0; k1 = 1; j0 = j1 = 0; n0 = n1 = 0; turn = 0;
+    nkb0 = k0 < units ? item_geom(unit_item(a, cache, k0), a.window).nkb : 1;
+    nkb1 = k1 < units ? item_geom(unit_item(a, cache, k1), a.window).nkb : 1;
   }
   // Next step: slot, unit index k within the CTA, block j, its unit's block
   // count and the slot's running step count c.  False when both are done.
-  __device__ __forceinline__ bool next(int& slot, int& kk, int& jj, int& nb, int& c) {
+  __device__ __forceinline__ bool next(const AttnArgs& a, const int4* cache, int& slot, int& kk, int& jj,
+                                       int& nb, int& c) {
     int s = turn;
-    if (k[s] >= units) s ^= 1;
-    if (k[s] >= units) return false;
-    slot = s; kk = k[s]; jj = j[s]; nb = nkb[s]; c = n[s];
-    ++n[s];
-    if (++j[s] == nkb[s]) {
-      j[s] = 0;
-      k[s] += 2;
-      load(s);
-    }
+    if ((s == 0 ? k0 : k1) >= units) s ^= 1;
+    if ((s == 0 ? k0 : k1) >= units) return false;
+    slot = s;
     turn = s ^ 1;
+    if (s == 0) {
+      kk = k0; jj = j0; nb = nkb0; c = n0++;
+      if (++j0 == nkb0) {
+        j0 = 0;
+        k0 += 2;
+        if (k0 < units) nkb0 = item_geom(unit_item(a, cache, k0), a.window).nkb;
+      }
+    } else {
+      kk = k1; jj = j1; nb = nkb1; c = n1++;
+      if (++j1 == nkb1) {
+        j1 = 0;
+        k1 += 2;
+        if (k1 < units) nkb1 = item_geom(unit_item(a, cache, k1), a.window).nkb;
+      }
+    }
     return true;
   }
 };
@@ -190,17 +254,30 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const A
   return mbar_wait_bounded(bar, parity, a.err, code, abort_flag, a.wait_limit_ns);
 }
 
+// Lane 0 waits (bounded) and the warp agrees on the outcome; a warp that
+// already failed does not wait again.
+__device__ __forceinline__ bool warp_wait(bool ok, uint64_t* bar, uint32_t parity, const AttnArgs& a,
+                                          volatile int* abort_flag) {
+  int w = ok ? 1 : 0;
+  if (ok && (threadIdx.x & 31) == 0) w = wait_bar(bar, parity, a, kErrAttnWait, abort_flag);
+  return __shfl_sync(0xffffffffu, w, 0) != 0;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
-    attn_flash_kernel(const __grid_constant__ CUtensorMap tm_qkv, const AttnArgs a) {
+    attn_flash_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  int4* uitems = reinterpret_cast<int4*>(smem + OFF_ITEMS);
+  float* xmax = reinterpret_cast<float*>(smem + OFF_XMAX);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* q_empty = q_full + 2;
-  uint64_t* kv_full = q_empty + 2;
-  uint64_t* kv_empty = kv_full + NKV;
-  uint64_t* s_full = kv_empty + NKV;
+  uint64_t* k_full = q_empty + 2;
+  uint64_t* k_empty = k_full + NK;
+  uint64_t* v_full = k_empty + NK;
+  uint64_t* v_empty = v_full + NV;
+  uint64_t* s_full = v_empty + NV;
   uint64_t* p_full = s_full + 2;
   uint64_t* pv_done = p_full + 2;
   uint64_t* drain = pv_done + 2;
@@ -210,19 +287,24 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total_units = a.num_items * 16;
-  const int my_units = blockIdx.x < total_units ? (total_units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  const int my_units =
+      static_cast<int>(blockIdx.x) < total_units ? (total_units - 1 - static_cast<int>(blockIdx.x)) / gridDim.x + 1 : 0;
 
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);  // the eight softmax warps of the slot
       mbar_init(&pv_done[i], 1);
     }
-    for (int i = 0; i < NKV; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+    for (int i = 0; i < NK; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < NV; ++i) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     mbar_init(drain, 1);
     mbar_init(stuck_bar, 1);  // nothing ever arrives on it (the timeout test)
@@ -230,10 +312,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
   }
-  if (warp == 1) {
+  // V rows past a sequence's end are never loaded: the V stages start as
+  // zeros (then only ever hold real, finite rows), so P = 0 times a stale row
+  // stays 0; the ones block feeds the row-sum columns of O
+  {
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    const uint4 one = make_uint4(0x3C003C00u, 0x3C003C00u, 0x3C003C00u, 0x3C003C00u);  // f16 1.0
+    for (int i = tid; i < (NV + 1) * TILE_BYTES / 16; i += THREADS)
+      reinterpret_cast<uint4*>(smem + OFF_V)[i] = i < NV * TILE_BYTES / 16 ? z : one;
+  }
+  // the work items come from the plan upload, which precedes every kernel of
+  // the forward, so they may be read before the previous kernel completes
+  if (tid >= 96 && tid - 96 < MAX_UNITS && tid - 96 < my_units)
+    uitems[tid - 96] = __ldg(a.items + ((blockIdx.x + (tid - 96) * gridDim.x) >> 4));
+  if (warp == 2) {
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
+  fence_proxy_async_smem();  // the zeros and ones, before the tensor core reads them
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -241,61 +337,81 @@ __global__ void __launch_bounds__(THREADS, 1)
   grid_dep_wait();
   grid_dep_trigger();
 
-  if (warp == 0) {
-    // ---- TMA producer ------------------------------------------------------------
+  if (warp <= 1) {
+    // ---- TMA producers: warp 0 Q and K, warp 1 V, both in the step order ------------
     if (lane == 0) {
       bool ok = true;
       if (a.stuck) ok = wait_bar(stuck_bar, 0, a, kErrAttnWait, abort_flag);
       const uint64_t pol = l2_evict_first();  // q/k/v are read by this launch only
       StepIter it;
-      it.init(&a, my_units);
-      uint32_t qe_phase[2] = {0, 0}, kve_phase = 0;
-      int nq[2] = {0, 0}, stage = 0;
+      it.init(a, uitems, my_units);
+      uint32_t qe_phase0 = 0, qe_phase1 = 0, e_phase = 0;
+      int nq0 = 0, nq1 = 0, stage = 0;
+      const int nst = warp == 0 ? NK : NV;
       int slot, kk, jj, nb, c;
-      while (ok && it.next(slot, kk, jj, nb, c)) {
-        const int u = blockIdx.x + kk * gridDim.x;
-        const int h = u & 15;
-        const ItemGeom g = item_geom(a.items[u >> 4], a.window);
-        if (jj == 0) {
-          if (nq[slot] > 0) {
-            if (!(ok = wait_bar(&q_empty[slot], qe_phase[slot], a, kErrAttnWait, abort_flag))) break;
-            qe_phase[slot] ^= 1u;
-          }
-          ++nq[slot];
-          mbar_arrive_expect_tx(&q_full[slot], TILE_BYTES);
-          tma_load_2d_hint(smem + OFF_Q + slot * TILE_BYTES, &tm_qkv, h * D, g.q_row0, &q_full[slot], pol);
-        }
-        if (!(ok = wait_bar(&kv_empty[stage], kve_phase ^ 1u, a, kErrAttnWait, abort_flag))) break;
-        uint8_t* kv = smem + OFF_KV + stage * KV_BYTES;
+      while (ok && it.next(a, uitems, slot, kk, jj, nb, c)) {
+        const int h = (static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x)) & 15;
+        const ItemGeom g = item_geom(unit_item(a, uitems, kk), a.window);
         const int krow = g.k_row0 + jj * TK;
-        mbar_arrive_expect_tx(&kv_full[stage], KV_BYTES);
-        tma_load_2d_hint(kv, &tm_qkv, 1024 + h * D, krow, &kv_full[stage], pol);
-        tma_load_2d_hint(kv + TILE_BYTES, &tm_qkv, 2048 + h * D, krow, &kv_full[stage], pol);
-        if (++stage == NKV) {
+        const int kb = boxes(krow, g.seq1);
+        if (warp == 0) {
+          if (jj == 0) {
+            if ((slot == 0 ? nq0 : nq1) > 0) {
+              uint32_t& ph = slot == 0 ? qe_phase0 : qe_phase1;
+              if (!(ok = wait_bar(&q_empty[slot], ph, a, kErrAttnWait, abort_flag))) break;
+              ph ^= 1u;
+            }
+            if (slot == 0) ++nq0; else ++nq1;
+            const int qb = boxes(g.q_row0, g.q_row0 + g.q_rows);
+            mbar_arrive_expect_tx(&q_full[slot], qb * BOX_BYTES);
+            for (int b = 0; b < qb; ++b)
+              tma_load_2d_hint(smem + OFF_Q + slot * TILE_BYTES + b * BOX_BYTES, &tm_qkv, h * D, g.q_row0 + b * BOX,
+                               &q_full[slot], pol);
+          }
+          if (!(ok = wait_bar(&k_empty[stage], e_phase ^ 1u, a, kErrAttnWait, abort_flag))) break;
+          mbar_arrive_expect_tx(&k_full[stage], kb * BOX_BYTES);
+          for (int b = 0; b < kb; ++b)
+            tma_load_2d_hint(smem + OFF_K + stage * TILE_BYTES + b * BOX_BYTES, &tm_qkv, 1024 + h * D,
+                             krow + b * BOX, &k_full[stage], pol);
+        } else {
+          if (!(ok = wait_bar(&v_empty[stage], e_phase ^ 1u, a, kErrAttnWait, abort_flag))) break;
+          mbar_arrive_expect_tx(&v_full[stage], kb * BOX_BYTES);
+          for (int b = 0; b < kb; ++b)
+            tma_load_2d_hint(smem + OFF_V + stage * TILE_BYTES + b * BOX_BYTES, &tm_qkv, 2048 + h * D,
+                             krow + b * BOX, &v_full[stage], pol);
+        }
+        if (++stage == nst) {
           stage = 0;
-          kve_phase ^= 1u;
+          e_phase ^= 1u;
         }
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp == 1) {
+  } else if (warp == 2) {
     // ---- MMA issuer ----------------------------------------------------------------
     if (lane == 0) {
       bool ok = true;
       StepIter it;
-      it.init(&a, my_units);
-      uint32_t qf_phase[2] = {0, 0}, kvf_phase = 0, pf_phase[2] = {0, 0};
-      int p_seen[2] = {0, 0};  // p_full completions consumed per slot
-      int stage = 0;
+      it.init(a, uitems, my_units);
+      uint32_t qf_phase0 = 0, qf_phase1 = 0, kf_phase = 0, vf_phase = 0, pf_phase0 = 0, pf_phase1 = 0;
+      int p_seen0 = 0, p_seen1 = 0;  // p_full completions consumed per slot
+      int kst = 0, vst = 0;
+      // descriptors: per-step operands are fixed offsets from these
+      const uint32_t ones = smem_u32(smem + OFF_ONES);
+      const uint64_t dq0 = umma_desc_sw128(smem_u32(smem + OFF_Q));
+      const uint64_t dk0 = umma_desc_sw128(smem_u32(smem + OFF_K));
+      const uint64_t dp0 = umma_desc_sw128(smem_u32(smem + OFF_P));
       // the step issued last, whose P.V follows the next S
-      bool pend = false;
-      int pend_slot = 0, pend_stage = 0, pend_c = 0;
-      bool pend_first = false;
+      bool pend = false, pend_first = false;
+      int pend_slot = 0, pend_c = 0;
+      // waits until slot s's p_full has completed `count` times
       auto wait_p = [&](int s, int count) {
-        while (ok && p_seen[s] < count) {
-          ok = wait_bar(&p_full[s], pf_phase[s], a, kErrAttnWait, abort_flag);
-          pf_phase[s] ^= 1u;
-          ++p_seen[s];
+        int& seen = s == 0 ? p_seen0 : p_seen1;
+        uint32_t& ph = s == 0 ? pf_phase0 : pf_phase1;
+        while (ok && seen < count) {
+          ok = wait_bar(&p_full[s], ph, a, kErrAttnWait, abort_flag);
+          ph ^= 1u;
+          ++seen;
         }
         return ok;
       };
@@ -303,49 +419,56 @@ __global__ void __launch_bounds__(THREADS, 1)
         // P_j of the pending step is written (and its O rescaled) once p_full
         // completes for the slot's (c + 1)-th time
         if (!wait_p(pend_slot, pend_c + 1)) return;
+        if (!(ok = wait_bar(&v_full[vst], vf_phase, a, kErrAttnWait, abort_flag))) return;
         tc_fence_after();
-        const uint32_t pa = smem_u32(smem + OFF_P + pend_slot * P_BYTES);
-        const uint32_t va = smem_u32(smem + OFF_KV + pend_stage * KV_BYTES + TILE_BYTES);
-        const uint32_t d = tmem + O_COL + pend_slot * D;
+        const uint32_t va = smem_u32(smem + OFF_V + vst * TILE_BYTES);
+        const uint64_t dv = desc_mn_sw128(va, ones - va);
+        const uint64_t dp = dp0 + static_cast<uint64_t>(pend_slot * (P_BYTES >> 4));
+        const uint32_t d = tmem + O_COL + pend_slot * 128;
 #pragma unroll
         for (int kk2 = 0; kk2 < TK / 16; ++kk2)
-          umma_f16(d, umma_desc_sw128(pa + (kk2 >> 2) * TILE_BYTES + (kk2 & 3) * 32),
-                   desc_mn_sw128(va + kk2 * 2048), IDESC_PV, (!pend_first || kk2 > 0) ? 1u : 0u);
-        umma_commit(&kv_empty[pend_stage]);
+          umma_f16(d, dp + static_cast<uint64_t>((kk2 >> 2) * (TILE_BYTES >> 4) + (kk2 & 3) * 2),
+                   dv + static_cast<uint64_t>(kk2 * (2048 >> 4)), IDESC_PV, (!pend_first || kk2 > 0) ? 1u : 0u);
+        umma_commit(&v_empty[vst]);
         umma_commit(&pv_done[pend_slot]);
+        if (++vst == NV) {
+          vst = 0;
+          vf_phase ^= 1u;
+        }
         pend = false;
       };
       int slot, kk, jj, nb, c;
-      while (ok && it.next(slot, kk, jj, nb, c)) {
+      while (ok && it.next(a, uitems, slot, kk, jj, nb, c)) {
         // S[slot] is free once the slot's previous step has its P written
         if (!wait_p(slot, c)) break;
         if (jj == 0) {
-          if (!(ok = wait_bar(&q_full[slot], qf_phase[slot], a, kErrAttnWait, abort_flag))) break;
-          qf_phase[slot] ^= 1u;
+          uint32_t& ph = slot == 0 ? qf_phase0 : qf_phase1;
+          if (!(ok = wait_bar(&q_full[slot], ph, a, kErrAttnWait, abort_flag))) break;
+          ph ^= 1u;
         }
-        if (!(ok = wait_bar(&kv_full[stage], kvf_phase, a, kErrAttnWait, abort_flag))) break;
+        if (!(ok = wait_bar(&k_full[kst], kf_phase, a, kErrAttnWait, abort_flag))) break;
         tc_fence_after();
-        const uint32_t qa = smem_u32(smem + OFF_Q + slot * TILE_BYTES);
-        const uint32_t ka = smem_u32(smem + OFF_KV + stage * KV_BYTES);
+        const uint64_t dq = dq0 + static_cast<uint64_t>(slot * (TILE_BYTES >> 4));
+        const uint64_t dk = dk0 + static_cast<uint64_t>(kst * (TILE_BYTES >> 4));
 #pragma unroll
         for (int k4 = 0; k4 < D / 16; ++k4)
-          umma_f16(tmem + S_COL + slot * TK, umma_desc_sw128(qa + k4 * 32), umma_desc_sw128(ka + k4 * 32), IDESC_QK,
-                   k4 > 0 ? 1u : 0u);
+          umma_f16(tmem + S_COL + slot * TK, dq + static_cast<uint64_t>(2 * k4), dk + static_cast<uint64_t>(2 * k4),
+                   IDESC_QK, k4 > 0 ? 1u : 0u);
         umma_commit(&s_full[slot]);
+        umma_commit(&k_empty[kst]);
         if (jj == nb - 1) umma_commit(&q_empty[slot]);
+        if (++kst == NK) {
+          kst = 0;
+          kf_phase ^= 1u;
+        }
         if (pend) {
           issue_pv();
           if (!ok) break;
         }
         pend = true;
         pend_slot = slot;
-        pend_stage = stage;
         pend_c = c;
         pend_first = jj == 0;
-        if (++stage == NKV) {
-          stage = 0;
-          kvf_phase ^= 1u;
-        }
       }
       if (ok && pend) issue_pv();
       if (!ok) *abort_flag = 1;
@@ -355,55 +478,57 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else {
     // ---- softmax warpgroups --------------------------------------------------------
-    const int slot = (warp - 2) >> 2;
+    const int wg = (warp - CTRL_WARPS) >> 2;
+    const int slot = wg >> 1, half = wg & 1;
     const int q = warp & 3;                     // TMEM lane quarter of this warp
     const int row = q * 32 + lane;              // query row within the item
+    const int bar_id = 1 + slot * 4 + q;        // this row quarter's two warps
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    const uint32_t t_s = t_lane + S_COL + slot * TK;
-    const uint32_t t_o = t_lane + O_COL + slot * D;
-    uint8_t* prow = smem + OFF_P + slot * P_BYTES + row * 128;
+    const uint32_t t_s = t_lane + S_COL + slot * TK + half * 64;  // this half's 64 keys
+    const uint32_t t_o = t_lane + O_COL + slot * 128 + half * 32;  // this half's 32 columns of O
+    const uint32_t t_sum = t_lane + O_COL + slot * 128 + D;       // the row-sum column
+    uint8_t* prow = smem + OFF_P + slot * P_BYTES + half * TILE_BYTES + row * 128;
+    float* xmax_s = xmax + slot * (2 * 2 * TQ);
     uint32_t sf_phase = 0, pv_phase = 0;
+    int par = 0;
     bool ok = true;
-    for (int kk = slot; kk < my_units && ok; kk += 2) {
-      const int u = blockIdx.x + kk * gridDim.x;
-      const int h = u & 15;
-      const ItemGeom g = item_geom(a.items[u >> 4], a.window);
+    for (int kk = slot; kk < my_units; kk += 2) {
+      const int h = (static_cast<int>(blockIdx.x) + kk * static_cast<int>(gridDim.x)) & 15;
+      const int4 it = unit_item(a, uitems, kk);
+      const ItemGeom g = item_geom(it, a.window);
       const bool valid = row < g.q_rows;
       const int r_abs = g.q_row0 + row;
       int lo = 0, hi = 0;  // visible keys, absolute rows
       if (valid) {
-        const int2 sp = a.rowspan[r_abs];
-        lo = sp.x;
-        hi = sp.y;
+        lo = it.z;
+        hi = g.seq1;
         if (a.window >= 0) {
           lo = r_abs - a.window > lo ? r_abs - a.window : lo;
           hi = r_abs + a.window + 1 < hi ? r_abs + a.window + 1 : hi;
         }
       }
-      float m_run = -INFINITY, l_run = 0.0f;
-      for (int jj = 0; jj < g.nkb && ok; ++jj) {
-        int w_ok = 1;
-        if (lane == 0) w_ok = wait_bar(&s_full[slot], sf_phase, a, kErrAttnWait, abort_flag);
+      float m_run = -INFINITY;
+      for (int jj = 0; jj < g.nkb; ++jj) {
+        ok = warp_wait(ok, &s_full[slot], sf_phase, a, abort_flag);
         sf_phase ^= 1u;
-        if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        // keys [a, b) of this block are visible to the row (block-relative)
-        const int kbase = g.k_row0 + jj * TK;
+        if (ok) tc_fence_after();
+        // keys [a0, b0) of this half's 64 are visible to the row
+        const int kbase = g.k_row0 + jj * TK + half * 64;
         const int a0 = lo - kbase, b0 = hi - kbase;
-        // pass 1: block maximum, streaming S from TMEM 32 keys at a time;
-        // a chunk no row of the warp can see is skipped (warp-uniformly)
+        const uint32_t mask0 = chunk_mask(a0, b0), mask1 = chunk_mask(a0 - 32, b0 - 32);
+        const bool any0 = __any_sync(0xffffffffu, mask0 != 0u), any1 = __any_sync(0xffffffffu, mask1 != 0u);
+        const bool all0 = __all_sync(0xffffffffu, mask0 == 0xffffffffu);
+        const bool all1 = __all_sync(0xffffffffu, mask1 == 0xffffffffu);
+        // pass 1: this half's maximum
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          const uint32_t mask = chunk_mask(a0 - 32 * ch, b0 - 32 * ch);
-          if (!__any_sync(0xffffffffu, mask != 0u)) continue;
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          const uint32_t mask = ch ? mask1 : mask0;
+          if (!ok || !(ch ? any1 : any0)) continue;
           uint32_t v[32];
           tmem_ld_32x32b_x32(t_s + 32 * ch, v);
           tmem_ld_wait();
-          if (__all_sync(0xffffffffu, mask == 0xffffffffu)) {
+          if (ch ? all1 : all0) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], u2f(v[j]));
           } else {
@@ -411,110 +536,114 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], (mask >> j) & 1u ? u2f(v[j]) : -INFINITY);
           }
         }
-        const float mb = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-        const float m_new = fmaxf(m_run, mb);
+        const float mh = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        // the row's block maximum: this half's and the other half's
+        xmax_s[(par * 2 + half) * TQ + row] = mh;
+        named_sync(bar_id, 64);
+        const float mo = xmax_s[(par * 2 + (half ^ 1)) * TQ + row];
+        par ^= 1;
+        const float m_new = fmaxf(m_run, fmaxf(mh, mo));
         const float m_use = m_new == -INFINITY ? 0.0f : m_new;
         const float ms = m_use * L2E;
-        // O and l were accumulated against m_run: rescale by 2^((m_run - m_new) log2 e)
+        // O (sums included) was accumulated against m_run: rescale by
+        // 2^((m_run - m_new) log2 e)
         const float alpha = m_run == -INFINITY ? 0.0f : fast_exp2((m_run - m_use) * L2E);
         // the slot's previous P.V must be done: P is rewritten and O rescaled
         if (jj > 0) {
-          int v_ok = 1;
-          if (lane == 0) v_ok = wait_bar(&pv_done[slot], pv_phase, a, kErrAttnWait, abort_flag);
+          ok = warp_wait(ok, &pv_done[slot], pv_phase, a, abort_flag);
           pv_phase ^= 1u;
-          if (!__shfl_sync(0xffffffffu, v_ok, 0)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
+          if (ok) tc_fence_after();
         }
         // pass 2: P = 2^(s log2e - max) (0 where hidden) as f16 into this
-        // row of P (chunk ch -> K atom ch / 2, 16-byte chunks 4 (ch % 2) ..)
-        float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll 1
-        for (int ch = 0; ch < 4; ++ch) {
-          const uint32_t mask = chunk_mask(a0 - 32 * ch, b0 - 32 * ch);
-          uint32_t w[16];
-          if (!__any_sync(0xffffffffu, mask != 0u)) {
+        // half's atom of the row (chunk ch -> 16-byte chunks 4 ch .. 4 ch + 3)
+        if (ok) {
 #pragma unroll
-            for (int j = 0; j < 16; ++j) w[j] = 0u;
-          } else {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(t_s + 32 * ch, v);
-            tmem_ld_wait();
-            float p[32];
-            if (__all_sync(0xffffffffu, mask == 0xffffffffu)) {
+          for (int ch = 0; ch < 2; ++ch) {
+            const uint32_t mask = ch ? mask1 : mask0;
+            uint32_t w[16];
+            if (!(ch ? any1 : any0)) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) p[j] = fast_exp2(fmaf(u2f(v[j]), L2E, -ms));
+              for (int j = 0; j < 16; ++j) w[j] = 0u;
             } else {
+              uint32_t v[32];
+              tmem_ld_32x32b_x32(t_s + 32 * ch, v);
+              tmem_ld_wait();
+              if (ch ? all1 : all0) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                p[j] = fast_exp2((mask >> j) & 1u ? fmaf(u2f(v[j]), L2E, -ms) : -INFINITY);
+                for (int j = 0; j < 32; j += 2)
+                  w[j / 2] = exp2_h2(fmaf(u2f(v[j]), L2E, -ms), fmaf(u2f(v[j + 1]), L2E, -ms));
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; j += 2)
+                  w[j / 2] = exp2_h2((mask >> j) & 1u ? fmaf(u2f(v[j]), L2E, -ms) : -INFINITY,
+                                     (mask >> (j + 1)) & 1u ? fmaf(u2f(v[j + 1]), L2E, -ms) : -INFINITY);
+              }
             }
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              sm[(j >> 1) & 3] += p[j] + p[j + 1];
-              w[j / 2] = pack_half2(p[j], p[j + 1]);
-            }
+            for (int x = 0; x < 4; ++x)
+              *reinterpret_cast<uint4*>(prow + (((4 * ch + x) ^ (row & 7)) << 4)) =
+                  make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
           }
-          uint8_t* pr = prow + (ch >> 1) * TILE_BYTES;
-          const int c0 = (ch & 1) * 4;
-#pragma unroll
-          for (int x = 0; x < 4; ++x)
-            *reinterpret_cast<uint4*>(pr + (((c0 + x) ^ (row & 7)) << 4)) =
-                make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
         }
-        const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
-        l_run = jj == 0 ? sum : l_run * alpha + sum;
         // tcgen05.ld / st are warp-collective (.sync.aligned): the whole warp
-        // rescales when any of its rows' maximum grew (alpha is 1 elsewhere)
-        if (jj > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
+        // rescales when any of its rows' maximum grew (alpha is 1 elsewhere);
+        // half 1 also rescales the row-sum column
+        if (ok && jj > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
           uint32_t o[32];
+          tmem_ld_32x32b_x32(t_o, o);
+          uint32_t sv = 0;
+          if (half) sv = tmem_ld_32x32b_x1(t_sum);
+          tmem_ld_wait();
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            tmem_ld_32x32b_x32(t_o + 32 * hh, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(u2f(o[j]) * alpha);
-            tmem_st_32x32b_x32(t_o + 32 * hh, o);
-          }
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(u2f(o[j]) * alpha);
+          tmem_st_32x32b_x32(t_o, o);
+          if (half) tmem_st_32x32b_x1(t_sum, __float_as_uint(u2f(sv) * alpha));
           tmem_st_wait();
         }
         m_run = m_new;
         fence_proxy_async_smem();  // P (generic writes) visible to the tensor core
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&p_full[slot]);
+        if (lane == 0 && ok) mbar_arrive(&p_full[slot]);
       }
-      if (!ok) break;
-      // the unit's last P.V, then the epilogue
-      int v_ok = 1;
-      if (lane == 0) v_ok = wait_bar(&pv_done[slot], pv_phase, a, kErrAttnWait, abort_flag);
+      // the unit's last P.V, then the epilogue: each half scales its 32 of
+      // the row's 64 values by 1 / (row sum) and stages them as f16 in the
+      // slot's P buffer (free now: its last P.V is done), row r at r * 128
+      // bytes, 16-byte chunk c at (c ^ (r & 7)); then the row quarter's two
+      // warps store their 32 rows with whole 128-byte lines per row
+      ok = warp_wait(ok, &pv_done[slot], pv_phase, a, abort_flag);
       pv_phase ^= 1u;
-      if (!__shfl_sync(0xffffffffu, v_ok, 0)) {
-        ok = false;
-        break;
+      uint8_t* stage = smem + OFF_P + slot * P_BYTES;
+      if (ok) {
+        tc_fence_after();
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(t_o, o);
+        const uint32_t sv = tmem_ld_32x32b_x1(t_sum);
+        tmem_ld_wait();
+        const float l = u2f(sv);
+        const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+          *reinterpret_cast<uint4*>(stage + row * 128 + (((4 * half + x) ^ (row & 7)) << 4)) =
+              make_uint4(pack_half2(u2f(o[8 * x]) * inv, u2f(o[8 * x + 1]) * inv),
+                         pack_half2(u2f(o[8 * x + 2]) * inv, u2f(o[8 * x + 3]) * inv),
+                         pack_half2(u2f(o[8 * x + 4]) * inv, u2f(o[8 * x + 5]) * inv),
+                         pack_half2(u2f(o[8 * x + 6]) * inv, u2f(o[8 * x + 7]) * inv));
       }
-      tc_fence_after();
-      uint32_t o0[32], o1[32];
-      tmem_ld_32x32b_x32(t_o, o0);
-      tmem_ld_32x32b_x32(t_o + 32, o1);
-      tmem_ld_wait();
-      if (valid) {
-        const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(r_abs) * 1024 + h * D);
+      named_sync(bar_id, 64);
+      if (ok) {
+        // 32 rows x 8 chunks of this quarter; thread i of the pair takes
+        // chunks i, i + 64, i + 128, i + 192 (8 consecutive threads per row)
+        const int i = half * 32 + lane;
 #pragma unroll
-        for (int x = 0; x < 4; ++x)
-          dst[x] = make_uint4(pack_half2(u2f(o0[8 * x]) * inv, u2f(o0[8 * x + 1]) * inv),
-                              pack_half2(u2f(o0[8 * x + 2]) * inv, u2f(o0[8 * x + 3]) * inv),
-                              pack_half2(u2f(o0[8 * x + 4]) * inv, u2f(o0[8 * x + 5]) * inv),
-                              pack_half2(u2f(o0[8 * x + 6]) * inv, u2f(o0[8 * x + 7]) * inv));
-#pragma unroll
-        for (int x = 0; x < 4; ++x)
-          dst[4 + x] = make_uint4(pack_half2(u2f(o1[8 * x]) * inv, u2f(o1[8 * x + 1]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 2]) * inv, u2f(o1[8 * x + 3]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 4]) * inv, u2f(o1[8 * x + 5]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 6]) * inv, u2f(o1[8 * x + 7]) * inv));
+        for (int x = 0; x < 4; ++x) {
+          const int cidx = i + 64 * x;
+          const int rr = q * 32 + (cidx >> 3), c = cidx & 7;
+          if (rr < g.q_rows) {
+            const uint4 vv = *reinterpret_cast<const uint4*>(stage + rr * 128 + ((c ^ (rr & 7)) << 4));
+            *reinterpret_cast<uint4*>(a.out + static_cast<size_t>(g.q_row0 + rr) * 1024 + h * D + c * 8) = vv;
+          }
+        }
       }
       tc_fence_before();  // O read before the slot's next unit overwrites it
     }
@@ -530,7 +659,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     while (global_ns() - t0 < 2000000ull) __nanosleep(1000);
   }
   __syncthreads();
-  if (warp == 1) {
+  if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -540,7 +669,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_sms, cudaStream_t stream) {
   if (a.num_items <= 0) return cudaSuccess;
-  if (!a.items || !a.rowspan || !a.out || !a.err || num_sms <= 0) return cudaErrorInvalidValue;
+  if (!a.items || !a.out || !a.err || num_sms <= 0) return cudaErrorInvalidValue;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

@@ -70,25 +70,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread in hardware for up to `hint_ns`
+// (woken as soon as the phase completes), so a waiting warp issues no
+// instructions while it waits instead of spinning on the barrier.
+constexpr uint32_t kSuspendHintNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with the given parity to complete.  Returns false (and
 // records `code` in *err) when the wall-clock limit passes (limit_ns, or
 // kWaitLimitNs when 0) or when *abort (a shared-memory flag other roles
-// raise on their own failure) is set.
+// raise on their own failure) is set.  Each try suspends the thread for at
+// most kSuspendHintNs, so the limit and the abort flag are checked at least
+// that often.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
                                                   int code, volatile int* abort_flag,
                                                   unsigned long long limit_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long limit = limit_ns ? limit_ns : kWaitLimitNs;
   const unsigned long long t0 = global_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (abort_flag && *abort_flag) return false;
-      if (global_ns() - t0 > limit) {
-        atomicCAS(err, 0, code);
-        if (abort_flag) *abort_flag = 1;
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_suspend(bar, parity)) return true;
+    if (abort_flag && *abort_flag) return false;
+    if (global_ns() - t0 > limit) {
+      atomicCAS(err, 0, code);
+      if (abort_flag) *abort_flag = 1;
+      return false;
     }
   }
 }

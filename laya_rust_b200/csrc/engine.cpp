@@ -186,9 +186,10 @@ struct Weight {
 // Host-side plan of one request: validated and compacted (real tokens only).
 // Rows [row0, row0 + rows) of the compacted batch (whole sequences) whose
 // encoder and head layers run as one chain of launches; its attention work
-// items are items[item0, item0 + nitems).
+// is tiles[tile0, tile0 + ntiles) (packed sequences of at most kAttnTcQRows
+// tokens) and items[item0, item0 + nitems) (128-row blocks of longer ones).
 struct RowGroup {
-  int row0 = 0, rows = 0, item0 = 0, nitems = 0;
+  int row0 = 0, rows = 0, tile0 = 0, ntiles = 0, item0 = 0, nitems = 0;
 };
 
 // With LAYA_ROW_GROUPS=2, batches of at least kSplitMinRows real tokens run as
@@ -238,11 +239,10 @@ int splitk_max() {
 }
 
 struct HostPlan {
-  int n = 0, l = 0, k = 0, R = 0, nitems = 0;
-  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row;
-  // (first row, end row) of each row's sequence
-  std::vector<int2> rowspan;
-  // attention work items per row group (see attention_items)
+  int n = 0, l = 0, k = 0, R = 0, ntiles = 0, nitems = 0;
+  std::vector<int> tok, pos, seq_start, seq_len, cls_row, mk_row, rowseq;
+  // attention work per row group (see pack_short_tiles, attention_items)
+  std::vector<int2> tiles;
   std::vector<int4> items;
   std::vector<RowGroup> groups;
   std::vector<uint8_t> rowtype;
@@ -251,7 +251,7 @@ struct HostPlan {
 
 // Offsets of each array inside one packed device buffer.
 struct PlanLayout {
-  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, items, rowtype, mmask, rowspan, total;
+  size_t tok, pos, seq_start, seq_len, cls_row, mk_row, tiles, items, rowtype, mmask, rowseq, total;
 };
 
 size_t up256(size_t x) { return (x + 255) / 256 * 256; }
@@ -270,10 +270,11 @@ PlanLayout layout_for(const HostPlan& p) {
   L.seq_len = take(sizeof(int) * p.n);
   L.cls_row = take(sizeof(int) * p.n);
   L.mk_row = take(sizeof(int) * p.n * p.k);
+  L.tiles = take(sizeof(int2) * p.ntiles);
   L.items = take(sizeof(int4) * p.nitems);
   L.rowtype = take(p.R);
   L.mmask = take((size_t)p.n * p.k);
-  L.rowspan = take(sizeof(int2) * p.R);
+  L.rowseq = take(sizeof(int) * p.R);
   L.total = o;
   return L;
 }
@@ -285,49 +286,50 @@ void pack(const HostPlan& p, const PlanLayout& L, uint8_t* dst) {
   memcpy(dst + L.seq_len, p.seq_len.data(), sizeof(int) * p.n);
   memcpy(dst + L.cls_row, p.cls_row.data(), sizeof(int) * p.n);
   memcpy(dst + L.mk_row, p.mk_row.data(), sizeof(int) * p.n * p.k);
+  memcpy(dst + L.tiles, p.tiles.data(), sizeof(int2) * p.ntiles);
   memcpy(dst + L.items, p.items.data(), sizeof(int4) * p.nitems);
   memcpy(dst + L.rowtype, p.rowtype.data(), p.R);
   memcpy(dst + L.mmask, p.mmask.data(), (size_t)p.n * p.k);
-  memcpy(dst + L.rowspan, p.rowspan.data(), sizeof(int2) * p.R);
+  memcpy(dst + L.rowseq, p.rowseq.data(), sizeof(int) * p.R);
 }
 
-// Attention work items for the sequences [b0, b1): int4 (first query row,
-// query rows, sequence start row, sequence length).  First the 128-row
-// blocks of sequences longer than kAttnTcQRows, longest sequences first (they
-// see the most key blocks, so the persistent kernel's round-robin deals them
-// out first); then tiles packing consecutive shorter sequences (adjacent in
-// the compacted rows) while their rows fit in kAttnTcQRows, each tile one
-// item whose "sequence" is the tile itself (its rows still see only their
-// own sequence's keys, through the row spans).
-void attention_items(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
-                     std::vector<int4>& out) {
-  std::vector<int> longs;
-  for (int b = b0; b < b1; ++b)
-    if (len[b] > kAttnTcQRows) longs.push_back(b);
-  std::stable_sort(longs.begin(), longs.end(), [&](int x, int y) { return len[x] > len[y]; });
-  for (int b : longs)
-    for (int q0 = 0; q0 < len[b]; q0 += kAttnTcQRows)
-      out.push_back(make_int4(start[b] + q0, std::min(kAttnTcQRows, len[b] - q0), start[b], len[b]));
+// Attention tiles for the sequences of at most kAttnTcQRows tokens among
+// [b0, b1): consecutive ones (adjacent in the compacted rows) share a tile
+// while their rows fit, as (first row, rows).
+void pack_short_tiles(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
+                      std::vector<int2>& out) {
   int row0 = -1, rows = 0;
-  auto flush = [&] {
-    if (row0 >= 0) out.push_back(make_int4(row0, rows, row0, rows));
-    row0 = -1;
-    rows = 0;
-  };
   for (int b = b0; b < b1; ++b) {
     if (len[b] > kAttnTcQRows) {
-      flush();
+      if (row0 >= 0) out.push_back(make_int2(row0, rows));
+      row0 = -1;
       continue;
     }
     if (row0 >= 0 && start[b] == row0 + rows && rows + len[b] <= kAttnTcQRows) {
       rows += len[b];
     } else {
-      flush();
+      if (row0 >= 0) out.push_back(make_int2(row0, rows));
       row0 = start[b];
       rows = len[b];
     }
   }
-  flush();
+  if (row0 >= 0) out.push_back(make_int2(row0, rows));
+}
+
+// Flash-attention work items for the sequences longer than kAttnTcQRows
+// tokens among [b0, b1): int4 (first query row, query rows, sequence start
+// row, sequence length), one per block of kAttnTcQRows query rows, longest
+// sequences first (they see the most key blocks, so the persistent kernel's
+// round-robin deals them out first; ties keep sequence order).
+void attention_items(const std::vector<int>& start, const std::vector<int>& len, int b0, int b1,
+                     std::vector<int4>& out) {
+  std::vector<int> order;
+  for (int b = b0; b < b1; ++b)
+    if (len[b] > kAttnTcQRows) order.push_back(b);
+  std::stable_sort(order.begin(), order.end(), [&](int x, int y) { return len[x] > len[y]; });
+  for (int b : order)
+    for (int q0 = 0; q0 < len[b]; q0 += kAttnTcQRows)
+      out.push_back(make_int4(start[b] + q0, std::min(kAttnTcQRows, len[b] - q0), start[b], len[b]));
 }
 
 // Validates a Req and compacts its real tokens.  The reference asserts
@@ -368,7 +370,7 @@ HostPlan make_plan(const laya_req* q) {
   p.tok.resize(R);
   p.pos.resize(R);
   p.rowtype.resize(R);
-  p.rowspan.resize(R);
+  p.rowseq.resize(R);
   for (int b = 0; b < p.n; ++b) {
     const int64_t* ids = q->ids + (size_t)b * p.l;
     for (int t = 0; t < p.l; ++t)
@@ -378,7 +380,7 @@ HostPlan make_plan(const laya_req* q) {
       p.tok[p.seq_start[b] + t] = (int)ids[t];
       p.pos[p.seq_start[b] + t] = t;
       p.rowtype[p.seq_start[b] + t] = (uint8_t)q->qtype[b];
-      p.rowspan[p.seq_start[b] + t] = make_int2(p.seq_start[b], p.seq_start[b] + p.seq_len[b]);
+      p.rowseq[p.seq_start[b] + t] = b;
     }
   }
   // two row groups of about R/2 rows, split at a sequence boundary
@@ -399,11 +401,15 @@ HostPlan make_plan(const laya_req* q) {
     const int b0 = bounds[gi], b1 = bounds[gi + 1];
     g.row0 = p.seq_start[b0];
     g.rows = (b1 < p.n ? p.seq_start[b1] : R) - g.row0;
+    g.tile0 = (int)p.tiles.size();
+    pack_short_tiles(p.seq_start, p.seq_len, b0, b1, p.tiles);
+    g.ntiles = (int)p.tiles.size() - g.tile0;
     g.item0 = (int)p.items.size();
     attention_items(p.seq_start, p.seq_len, b0, b1, p.items);
     g.nitems = (int)p.items.size() - g.item0;
     p.groups.push_back(g);
   }
+  p.ntiles = (int)p.tiles.size();
   p.nitems = (int)p.items.size();
   p.cls_row.resize(p.n);
   p.mk_row.resize((size_t)p.n * p.k);
@@ -440,7 +446,8 @@ struct GroupMaps {
 struct PlanMaps {
   GroupMaps g[2];
   CUtensorMap a_mk;                                // scorer A operand (gathered marker rows)
-  CUtensorMap qkv_tiles;                           // attention: 64-column x 128-row boxes of qkv
+  CUtensorMap qkv_tiles;                           // short-sequence attention: 64-column x 128-row boxes of qkv
+  CUtensorMap qkv_rows;                            // flash attention: 64-column x 32-row boxes of qkv
   uint64_t gen = ~0ull;                            // arena generation encoded for
 };
 
@@ -732,7 +739,8 @@ struct Engine {
     const uint64_t R = (uint64_t)p.R, nk = (uint64_t)p.n * p.k;
     const uint32_t ab = kGemmABoxRows, ob = kGemmOutBoxRows;
     bool bad = make_tmap_f16(&m.a_mk, mk16.p, nk, H, ab) != 0 ||
-               make_tmap_2d(&m.qkv_tiles, qkv.p, false, R, 3 * H, 64, kAttnTcQRows) != 0;
+               make_tmap_2d(&m.qkv_tiles, qkv.p, false, R, 3 * H, 64, kAttnTcQRows) != 0 ||
+               make_tmap_2d(&m.qkv_rows, qkv.p, false, R, 3 * H, 64, kAttnTcBoxRows) != 0;
     for (size_t g = 0; g < p.groups.size() && !bad; ++g) {
       // each group's maps start at its first row and end at its last, so its
       // TMA stores never reach the other group's rows
@@ -776,28 +784,49 @@ struct Engine {
     mark(kind);
   }
 
-  // Attention over the group's sequences: one launch of the flash kernel
-  // over the group's work items.
+  // Attention over the group's sequences: one launch for the tiles of
+  // sequences of at most 128 tokens (single pass) and one of the flash
+  // kernel for longer ones.
   void attention(const DevicePlan& dp, int gi, int window, cudaStream_t s, int64_t& nl) {
     const RowGroup& g = dp.host.groups[gi];
     const PlanLayout& L = dp.lay;
-    AttnArgs aa{};
-    aa.out = ctx.as<__half>();
-    aa.items = dp.at<int4>(L.items) + g.item0;
-    aa.rowspan = dp.at<int2>(L.rowspan);
-    aa.num_items = g.nitems;
-    aa.window = window;
-    aa.err = err.as<int>();
-    if (stuck_next && stuck_kind == 1) {
-      // the timeout test: this launch's producers wait on a barrier nothing
-      // completes, for stuck_limit_ns, then the kernel unwinds and reports
-      aa.stuck = 1;
-      aa.wait_limit_ns = stuck_limit_ns;
-      stuck_next = false;
+    const bool stuck = stuck_next && stuck_kind == 1;
+    if (g.ntiles > 0) {
+      AttnShortArgs sa{};
+      sa.out = ctx.as<__half>();
+      sa.tiles = dp.at<int2>(L.tiles) + g.tile0;
+      sa.rowseq = dp.at<int>(L.rowseq);
+      sa.seq_start = dp.at<int>(L.seq_start);
+      sa.seq_len = dp.at<int>(L.seq_len);
+      sa.num_tiles = g.ntiles;
+      sa.window = window;
+      sa.err = err.as<int>();
+      if (stuck) {
+        // the timeout test: this launch's loads first wait on a barrier
+        // nothing completes, for stuck_limit_ns, then the kernel unwinds
+        sa.stuck = 1;
+        sa.wait_limit_ns = stuck_limit_ns;
+      }
+      ck(launch_attention_short(&dp.maps.qkv_tiles, sa, s), "attention");
+      ++nl;
+      mark(kProfAttn);
     }
-    ck(launch_attention_tc(&dp.maps.qkv_tiles, aa, num_sms, s), "attention");
-    ++nl;
-    mark(kProfAttn);
+    if (g.nitems > 0) {
+      AttnArgs aa{};
+      aa.out = ctx.as<__half>();
+      aa.items = dp.at<int4>(L.items) + g.item0;
+      aa.num_items = g.nitems;
+      aa.window = window;
+      aa.err = err.as<int>();
+      if (stuck) {
+        aa.stuck = 1;
+        aa.wait_limit_ns = stuck_limit_ns;
+      }
+      ck(launch_attention_tc(&dp.maps.qkv_rows, aa, num_sms, s), "attention");
+      ++nl;
+      mark(kProfAttn);
+    }
+    if (stuck) stuck_next = false;
   }
 
   // LayerNorm of row group gi's residual rows into `out`; first adds the
@@ -1641,33 +1670,51 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
       len[b] = lens[b];
       R += lens[b];
     }
+    std::vector<int2> tiles;
     std::vector<int4> items;
+    laya::pack_short_tiles(start, len, 0, n, tiles);
     laya::attention_items(start, len, 0, n, items);
-    std::vector<int2> span(R);
+    std::vector<int> rowseq(R);
     for (int b = 0; b < n; ++b)
-      for (int t = 0; t < len[b]; ++t) span[start[b] + t] = make_int2(start[b], start[b] + len[b]);
-    laya::DevBuf dq, dout, di, dsp, derr;
+      for (int t = 0; t < len[b]; ++t) rowseq[start[b] + t] = b;
+    laya::DevBuf dq, dout, dt, di, drs, ds, dl, derr;
     dq.alloc((size_t)R * 3072 * 2, "qkv");
     dout.alloc((size_t)R * 1024 * 2, "out");
-    di.alloc(items.size() * sizeof(int4), "items");
-    dsp.alloc((size_t)R * sizeof(int2), "rowspan");
+    dt.alloc(std::max<size_t>(1, tiles.size()) * sizeof(int2), "tiles");
+    di.alloc(std::max<size_t>(1, items.size()) * sizeof(int4), "items");
+    drs.alloc((size_t)R * 4, "rowseq");
+    ds.alloc((size_t)n * 4, "start");
+    dl.alloc((size_t)n * 4, "len");
     laya::ck(cudaMemcpy(dq.p, qkv, dq.bytes, cudaMemcpyHostToDevice), "h2d");
-    laya::ck(cudaMemcpy(di.p, items.data(), di.bytes, cudaMemcpyHostToDevice), "h2d");
-    laya::ck(cudaMemcpy(dsp.p, span.data(), dsp.bytes, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(dt.p, tiles.data(), tiles.size() * sizeof(int2), cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(di.p, items.data(), items.size() * sizeof(int4), cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(drs.p, rowseq.data(), (size_t)R * 4, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(ds.p, start.data(), (size_t)n * 4, cudaMemcpyHostToDevice), "h2d");
+    laya::ck(cudaMemcpy(dl.p, len.data(), (size_t)n * 4, cudaMemcpyHostToDevice), "h2d");
     laya::ck(cudaMemset(dout.p, 0, dout.bytes), "memset");
     derr.alloc(256, "err");
     laya::ck(cudaMemset(derr.p, 0, 256), "memset");
-    CUtensorMap tm;
-    if (laya::make_tmap_2d(&tm, dq.p, false, R, 3072, 64, laya::kAttnTcQRows))
+    CUtensorMap tm128, tm32;
+    if (laya::make_tmap_2d(&tm128, dq.p, false, R, 3072, 64, laya::kAttnTcQRows) ||
+        laya::make_tmap_2d(&tm32, dq.p, false, R, 3072, 64, laya::kAttnTcBoxRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed");
+    laya::AttnShortArgs sa{};
+    sa.out = dout.as<__half>();
+    sa.tiles = dt.as<int2>();
+    sa.rowseq = drs.as<int>();
+    sa.seq_start = ds.as<int>();
+    sa.seq_len = dl.as<int>();
+    sa.num_tiles = (int)tiles.size();
+    sa.window = window;
+    sa.err = derr.as<int>();
+    laya::ck(laya::launch_attention_short(&tm128, sa, 0), "attention launch");
     laya::AttnArgs a{};
     a.out = dout.as<__half>();
     a.items = di.as<int4>();
-    a.rowspan = dsp.as<int2>();
     a.num_items = (int)items.size();
     a.window = window;
     a.err = derr.as<int>();
-    laya::ck(laya::launch_attention_tc(&tm, a, num_sms, 0), "attention launch");
+    laya::ck(laya::launch_attention_tc(&tm32, a, num_sms, 0), "attention launch");
     laya::ck(cudaDeviceSynchronize(), "attention run");
     int ev = 0;
     laya::ck(cudaMemcpy(&ev, derr.p, 4, cudaMemcpyDeviceToHost), "d2h");

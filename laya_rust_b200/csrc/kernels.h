@@ -84,26 +84,43 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& maps, const GemmArgs& args
                         cudaStream_t stream, int bn = kGemmBN);
 
 // ---- attention over compacted sequences ----------------------------------------
-// Work items of 128 query rows (kAttnTcQRows): int4 (first query row, query
-// rows, first row of the sequence, sequence length).  A tile of whole
-// consecutive sequences of at most 128 tokens is one item with sequence
-// start = first row and length = rows (its rows see only their own
-// sequence, through rowspan); a longer sequence gives one item per 128-row
-// block.  Items whose queries see more key blocks come first.
+// Sequences longer than kAttnTcQRows (128) tokens: work items of at most 128
+// query rows of one sequence, int4 (first query row, query rows, first row
+// of the sequence, sequence length), one per 128-row block.  Items whose
+// queries see more key blocks come first.  q/k/v rows are loaded in boxes of
+// kAttnTcBoxRows rows, only those of the item's sequence.
 constexpr int kAttnTcQRows = 128;
+constexpr int kAttnTcBoxRows = 32;
 struct AttnArgs {
   __half* out;            // [R, 1024] context, token-major
   const int4* items;      // [num_items]
-  const int2* rowspan;    // [R] (first row, end row) of each row's sequence
   int num_items;
   int window;             // < 0: global
   int* err;               // device error word
   unsigned long long wait_limit_ns;  // 0: the default bound (2 s)
   int stuck;              // timeout test: the producer first waits on a barrier nothing completes
 };
-// tcgen05 flash attention (persistent, min(16 * items, num_sms) CTAs); tm_qkv
-// maps the qkv buffer ([R, 3072] f16, box 64 columns x 128 rows, 128-byte
-// swizzle): q at columns h*64, k at 1024 + h*64, v at 2048 + h*64.
+// Sequences of at most kAttnTcQRows tokens: tiles (first row, rows) packing
+// whole consecutive sequences, one CTA per (tile, head), single pass; each
+// row sees only its own sequence (rowseq, seq_start, seq_len).  tm_qkv: box
+// 64 columns x kAttnTcQRows rows.
+struct AttnShortArgs {
+  __half* out;            // [R, 1024]
+  const int2* tiles;      // [num_tiles]
+  const int* rowseq;      // [R] sequence of each row
+  const int* seq_start;   // [n]
+  const int* seq_len;     // [n]
+  int num_tiles;
+  int window;             // < 0: global
+  int* err;
+  unsigned long long wait_limit_ns;
+  int stuck;
+};
+cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArgs& a, cudaStream_t stream);
+
+// Longer sequences: tcgen05 flash attention (persistent, min(16 * items, num_sms) CTAs); tm_qkv
+// maps the qkv buffer ([R, 3072] f16, box 64 columns x kAttnTcBoxRows rows,
+// 128-byte swizzle): q at columns h*64, k at 1024 + h*64, v at 2048 + h*64.
 cudaError_t launch_attention_tc(const CUtensorMap* tm_qkv, const AttnArgs& a, int num_sms, cudaStream_t stream);
 
 // ---- row kernels -----------------------------------------------------------------
