@@ -70,6 +70,15 @@ int laya_upload_weight_f16(laya_engine *e, const char *name, const uint16_t *dat
                            const int64_t *stored_dims, int ndims);
 int laya_upload_weight_f32(laya_engine *e, const char *name, const float *data,
                            const int64_t *stored_dims, int ndims);
+/* Uploads one tensor exactly as the reference's unchanged loader hands it
+ * out: the values of Tensors::f32 with the dims of Tensors::dims
+ * (src/weights.rs:270-295), i.e. GRAPH layout, where the 120 matmul weights
+ * of arch::transpose_names (src/arch.rs:306-322) are transposed to [in, out].
+ * The engine transposes those back to the stored layout.  This is what the
+ * reference's CudaEngine::load uploads (src/backend/cuda/mod.rs:125-132), so
+ * a Rust shim can keep that loop unchanged. */
+int laya_upload_weight_f32_graph(laya_engine *e, const char *name, const float *data,
+                                 const int64_t *dims, int ndims);
 /* Checks that all 207 tensors are present. */
 int laya_finalize(laya_engine *e);
 

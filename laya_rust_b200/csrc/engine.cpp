@@ -23,6 +23,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <map>
+#include <set>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -150,6 +151,25 @@ std::map<std::string, Role> build_roles() {
   return r;
 }
 
+// The 120 weights Tensors::f32 transposes to graph layout (arch.rs:306-322):
+// every encoder layer's Wqkv, Wo, Wi and mlp.Wo, the head layers' in_proj,
+// linear1 and linear2, and the scorer's two linear weights.
+bool in_transpose_set(const std::string& name) {
+  static const std::set<std::string> names = [] {
+    std::set<std::string> s;
+    for (int i = 0; i < NLAYER; ++i)
+      for (const char* w : {"attn.Wqkv.weight", "attn.Wo.weight", "mlp.Wi.weight", "mlp.Wo.weight"})
+        s.insert(fmt("encoder.layers.%d.%s", i, w));
+    for (int i = 0; i < HEAD_LAYERS; ++i)
+      for (const char* w : {"self_attn.in_proj_weight", "linear1.weight", "linear2.weight"})
+        s.insert(fmt("head.layers.%d.%s", i, w));
+    s.insert("scorer.1.weight");
+    s.insert("scorer.3.weight");
+    return s;
+  }();
+  return names.count(name) > 0;
+}
+
 const std::map<std::string, Role>& roles() {
   static const std::map<std::string, Role> r = build_roles();
   return r;
@@ -221,6 +241,17 @@ constexpr int kPartRows = 4608;
 bool splitk_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("LAYA_SPLITK");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Large batches: a residual GEMM whose 256 x 256 tiles leave the last wave at
+// most half full splits the K loop of its last row blocks instead, so the
+// last wave is short (kEpiResidTail).  LAYA_TAILSPLIT=0 turns it off.
+bool tailsplit_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LAYA_TAILSPLIT");
     return !(v && v[0] == '0');
   }();
   return on;
@@ -641,6 +672,30 @@ struct Engine {
     wt.present = true;
   }
 
+  // A tensor as Tensors::f32 returns it (weights.rs:278-295): graph layout,
+  // i.e. the 120 matmul weights of the transpose set (arch.rs:306-322)
+  // transposed to [in, out] with dims as Tensors::dims reports them
+  // (weights.rs:270-276); every other tensor as stored.  Transposed back to
+  // the stored [out, in] layout, then uploaded like any stored tensor.
+  void upload_graph(const std::string& name, const float* data, const int64_t* dims, int nd) {
+    auto it = roles().find(name);
+    if (it == roles().end()) throw Error(LAYA_E_LOAD, "unknown tensor name " + name);
+    const std::vector<int64_t>& st = it->second.shape;
+    if (!in_transpose_set(name) || st.size() != 2) {
+      upload(name, data, false, dims, nd);
+      return;
+    }
+    if (nd != 2 || dims[0] != st[1] || dims[1] != st[0])
+      throw Error(LAYA_E_LOAD, fmt("tensor %s: graph-layout dims must be [%lld, %lld]", name.c_str(), (long long)st[1],
+                                   (long long)st[0]));
+    const size_t a = (size_t)st[0], c = (size_t)st[1];
+    std::vector<float> v(a * c);
+    // graph element (j, i) at j * a + i is stored element (i, j) at i * c + j
+    for (size_t i = 0; i < a; ++i)
+      for (size_t j = 0; j < c; ++j) v[i * c + j] = data[j * a + i];
+    upload(name, v.data(), false, st.data(), 2);
+  }
+
   static uint16_t f2h_or_copy(const void* data, bool is_f16, size_t i) {
     return is_f16 ? static_cast<const uint16_t*>(data)[i] : f2h_bits(static_cast<const float*>(data)[i]);
   }
@@ -719,6 +774,25 @@ struct Engine {
     parts_ready = true;
   }
 
+  // The split tail of a large residual GEMM of M rows: when its 256 x 256
+  // tiles fill more than one wave of clusters but leave the last one at most
+  // half full, the last tail_rb row blocks (covering those tiles) are cut
+  // into `splits` K parts (2..4, at least 4 k-blocks each, within the part
+  // region); splits < 2 means no tail split.
+  void choose_tail(int M, int K, int& tail_rb, int& splits) const {
+    tail_rb = 0;
+    splits = 1;
+    if (!parts_ready || !tailsplit_enabled()) return;
+    const int num_m = (M + kGemmBM - 1) / kGemmBM, num_n = H / kGemmBN, tiles = num_m * num_n;
+    const int clusters = num_sms / 2;
+    const int rem = tiles % clusters;
+    if (tiles <= clusters || rem == 0 || rem * 2 > clusters) return;
+    tail_rb = (rem + num_n - 1) / num_n;
+    int S = std::min(std::min(4, clusters / (tail_rb * num_n)), (K / kGemmBK) / 4);
+    while (S > 1 && S * tail_rb * kGemmBM > kPartRows) --S;
+    splits = S;
+  }
+
   // K parts for a residual GEMM of M rows: 1 (no split) unless its tiles
   // fill at most half the clusters; then as many as fill the clusters, at
   // least 4 k-blocks each, at most splitk_max(), within the part region.
@@ -762,7 +836,7 @@ struct Engine {
 
   // ---- the forward ---------------------------------------------------------------
   void gemm(int epi, const CUtensorMap& A, const Weight& Wt, const CUtensorMap& Out, int M, int N, int K, GemmArgs a,
-            cudaStream_t s, int64_t& nl, int kind) {
+            cudaStream_t s, int64_t& nl, int kind, const CUtensorMap* out2 = nullptr) {
     a.M = M;
     a.N = N;
     a.K = K;
@@ -777,7 +851,7 @@ struct Engine {
     // than 256 x 256 on the residual GEMMs: the smaller stages leave the TMA
     // latency exposed.  They stay available through launch_gemm's `bn`.
     const bool narrow = false;
-    ck(launch_gemm(epi, GemmMaps{&A, narrow ? &Wt.tmap_narrow : &Wt.tmap, &Out}, a, num_sms, s,
+    ck(launch_gemm(epi, GemmMaps{&A, narrow ? &Wt.tmap_narrow : &Wt.tmap, &Out, out2}, a, num_sms, s,
                    narrow ? kGemmBNNarrow : kGemmBN),
        "gemm launch");
     ++nl;
@@ -852,7 +926,20 @@ struct Engine {
     r.ldo = H;
     const int S = defer ? choose_splits(R, K) : 1;
     if (S < 2) {
-      gemm(kEpiResid, A, Wt, Out, R, H, K, r, s, nl, kind);
+      int tail_rb = 0, ts = 0;
+      if (defer) choose_tail(R, K, tail_rb, ts);
+      if (ts < 2) {
+        gemm(kEpiResid, A, Wt, Out, R, H, K, r, s, nl, kind);
+        return;
+      }
+      if (pend[gi].nparts > 0) throw Error(LAYA_E_STATE, "split-K parts of an earlier GEMM were not consumed");
+      const int num_m = (R + kGemmBM - 1) / kGemmBM, num_n = H / kGemmBN;
+      r.splits = ts;
+      r.main_tiles = (num_m - tail_rb) * num_n;
+      r.tail_row0 = (num_m - tail_rb) * kGemmBM;
+      r.split_rows = tail_rb * kGemmBM;
+      gemm(kEpiResidTail, A, Wt, Out, R, H, K, r, s, nl, kind, &parts_map[gi]);
+      pend[gi] = PendingParts{parts[gi].as<float>(), ts, (size_t)r.split_rows * H, r.tail_row0};
       return;
     }
     if (pend[gi].nparts > 0) throw Error(LAYA_E_STATE, "split-K parts of an earlier GEMM were not consumed");
@@ -1348,6 +1435,15 @@ int laya_upload_weight_f32(laya_engine* e, const char* name, const float* data, 
     if (!e || !name || !data || !dims || nd <= 0 || nd > 4) throw Error(LAYA_E_INVALID, "bad argument");
     e->e->set_device();
     e->e->upload(name, data, false, dims, nd);
+  });
+}
+
+int laya_upload_weight_f32_graph(laya_engine* e, const char* name, const float* data, const int64_t* dims,
+                                 int nd) {
+  return guard([&] {
+    if (!e || !name || !data || !dims || nd <= 0 || nd > 4) throw Error(LAYA_E_INVALID, "bad argument");
+    e->e->set_device();
+    e->e->upload_graph(name, data, dims, nd);
   });
 }
 

@@ -25,7 +25,10 @@
 //               (or TMA reduce-add for the f32 residual) of 32 rows at a time
 // With kEpiPartial (small M), a work unit is a (tile, K part) pair: the
 // clusters split each tile's K loop and store f32 part sums, which the next
-// row kernel adds in part order.
+// row kernel adds in part order.  With kEpiResidTail (a residual GEMM whose
+// tiles leave the last wave mostly idle), the tiles of whole waves add into
+// the residual stream and the tiles of the last row blocks are split into K
+// parts the same way, so the last wave is short.
 // No TMA load in this kernel uses multicast; every CTA loads its own operand
 // halves.  The MMA completion signal is delivered to both CTAs of the pair
 // with tcgen05.commit's cluster-multicast form.
@@ -226,12 +229,43 @@ struct Stager {
   }
 };
 
+// A persistent work unit: an output tile and the K range [kb0, kb1) of it
+// this unit accumulates; `part` is the K part (kEpiPartial, and the split
+// tail tiles of kEpiResidTail) and `tail` marks those tail units.
+struct Unit {
+  int tile, part, kb0, kb1;
+  bool tail;
+};
+
+template <int EPI>
+__device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a, int num_kb) {
+  Unit w{u, 0, 0, num_kb, false};
+  if constexpr (EPI == kEpiPartial) {
+    const int S = a.splits;
+    w.tile = u / S;
+    w.part = u - w.tile * S;
+    w.kb0 = w.part * num_kb / S;
+    w.kb1 = (w.part + 1) * num_kb / S;
+  } else if constexpr (EPI == kEpiResidTail) {
+    if (u >= a.main_tiles) {
+      const int S = a.splits, v = u - a.main_tiles;
+      w.tile = a.main_tiles + v / S;
+      w.part = v - (v / S) * S;
+      w.kb0 = w.part * num_kb / S;
+      w.kb1 = (w.part + 1) * num_kb / S;
+      w.tail = true;
+    }
+  }
+  return w;
+}
+
 // Epilogue of one warp: 32 rows (TMEM lanes) and column half `hc` of the
 // tile, i.e. columns [hc*BN/2, (hc+1)*BN/2) (for GeGLU: output columns
 // [hc*BN/4, (hc+1)*BN/4), from gate and up columns of that range).
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmOut, Stager& st,
-                                              uint32_t t_row, int row0, int row, int n0, int hc, int yoff) {
+                                              uint32_t t_row, int row0, int row, int n0, int hc, int yoff,
+                                              bool reduce) {
   const bool valid = row < a.M;
   const int r = row - row0;  // row within this warp's 32-row slab
   const int cb = hc * (BN / 2), ce = cb + BN / 2;
@@ -310,7 +344,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       stage_row(s, r, w);
       st.store(tmOut, n0 + c0, row0, false);
     }
-  } else if constexpr (EPI == kEpiResid || EPI == kEpiStoreF32 || EPI == kEpiPartial) {
+  } else if constexpr (EPI == kEpiResid || EPI == kEpiStoreF32 || EPI == kEpiPartial || EPI == kEpiResidTail) {
 #pragma unroll 1
     for (int c0 = cb; c0 < ce; c0 += 32) {
       uint32_t v[32];
@@ -323,8 +357,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       }
       uint8_t* s = st.acquire();
       stage_row(s, r, v);
-      // a part's rows start at yoff (kEpiPartial); 0 otherwise
-      st.store(tmOut, n0 + c0, row0 + yoff, EPI == kEpiResid);
+      // a part's rows start at yoff (K parts); 0 otherwise.  `reduce`: add
+      // into the residual stream instead of storing
+      st.store(tmOut, n0 + c0, row0 + yoff, reduce);
     }
   } else if constexpr (EPI == kEpiGeglu) {
     const int oc0 = (n0 / BN) * (BN / 2);
@@ -366,7 +401,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
 template <int EPI, int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmOut, const GemmArgs args) {
+                   const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
+                   const GemmArgs args) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -394,10 +430,12 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int num_n = args.N / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = args.K / BK;
-  // work unit u = (tile u / S, K part u % S): part p covers k-blocks
-  // [p * num_kb / S, (p + 1) * num_kb / S).  S = 1 except for kEpiPartial.
-  const int S = EPI == kEpiPartial ? args.splits : 1;
-  const int num_units = num_tiles * S;
+  // work units (unit_of): one per tile, or per (tile, K part) for
+  // kEpiPartial and for the tail tiles of kEpiResidTail; part p of S covers
+  // k-blocks [p * num_kb / S, (p + 1) * num_kb / S)
+  const int num_units = EPI == kEpiPartial    ? num_tiles * args.splits
+                        : EPI == kEpiResidTail ? args.main_tiles + (num_tiles - args.main_tiles) * args.splits
+                                               : num_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -442,11 +480,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       // at about the same time, and not after: evict-first
       const uint64_t pol_a = l2_evict_first();
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        const int tile = u / S, part = u - tile * S;
-        const int m0 = (tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
-        const int n0 = (tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
-        const int kb1 = (part + 1) * num_kb / S;
-        for (int kb = part * num_kb / S; kb < kb1; ++kb) {
+        const Unit w = unit_of<EPI>(u, args, num_kb);
+        const int m0 = (w.tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
+        const int n0 = (w.tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag,
                                  args.wait_limit_ns)) {
             ok = false;
@@ -478,8 +515,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t aphase = 0;
       bool ok = true;
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
-        const int part = u % S;
-        const int kb0 = part * num_kb / S, kb1 = (part + 1) * num_kb / S;
+        const Unit w = unit_of<EPI>(u, args, num_kb);
+        const int kb0 = w.kb0, kb1 = w.kb1;
         if (!mbar_wait_bounded(&tempty[acc], aphase ^ 1u, args.err, kErrGemmMmaWait, abort_flag, args.wait_limit_ns)) {
           ok = false;
           break;
@@ -522,7 +559,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t aphase = 0;
     for (int u = cluster_id; u < num_units; u += num_clusters) {
-      const int tile = u / S, part = u - tile * S;
+      const Unit w = unit_of<EPI>(u, args, num_kb);
+      const int tile = w.tile;
       int ok = 1;
       if (lane == 0)
         ok = mbar_wait_bounded(&tfull[acc], aphase, args.err, kErrGemmEpilogueWait, abort_flag, args.wait_limit_ns);
@@ -534,8 +572,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row0 = m0 + q * 32;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       st.active = row0 < args.M;
-      epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc,
-                             EPI == kEpiPartial ? part * args.split_rows : 0);
+      if constexpr (EPI == kEpiResidTail) {
+        // whole tiles add into the residual stream; a tail tile's part
+        // stores its sums in the parts region, rows counted from tail_row0
+        if (w.tail)
+          epilogue_tile<EPI, BN>(args, &tmOut2, st, t_row, row0, row0 + lane, n0, hc,
+                                 w.part * args.split_rows - args.tail_row0, false);
+        else
+          epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc, 0, true);
+      } else {
+        epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc,
+                               EPI == kEpiPartial ? w.part * args.split_rows : 0, EPI == kEpiResid);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
@@ -569,7 +617,9 @@ cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cud
   }
   const int num_tiles = ((args.M + BM - 1) / BM) * (args.N / BN);
   if (num_tiles == 0) return cudaSuccess;
-  const int num_units = num_tiles * (EPI == kEpiPartial ? args.splits : 1);
+  const int num_units = EPI == kEpiPartial    ? num_tiles * args.splits
+                        : EPI == kEpiResidTail ? args.main_tiles + (num_tiles - args.main_tiles) * args.splits
+                                               : num_tiles;
   const int max_clusters = num_sms / 2;
   const int clusters = num_units < max_clusters ? num_units : max_clusters;
   cudaLaunchAttribute attr[1];
@@ -578,7 +628,7 @@ cudaError_t launch_one(const GemmMaps& m, const GemmArgs& args, int num_sms, cud
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   return launch_pdl(gemm_tc_kernel<EPI, BN>, dim3(2 * clusters, 1, 1), dim3(THREADS, 1, 1), Cfg<BN>::SMEM, stream,
-                    attr, 1, *m.a, *m.b, *m.out, args);
+                    attr, 1, *m.a, *m.b, *m.out, m.out2 ? *m.out2 : *m.out, args);
 }
 
 }  // namespace
@@ -591,6 +641,16 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
       (bn != kGemmBN || args.splits < 1 || args.splits > args.K / BK || args.split_rows % BM ||
        args.split_rows < ((args.M + BM - 1) / BM) * BM))
     return cudaErrorInvalidValue;
+  if (epilogue == kEpiResidTail) {
+    // whole row blocks before the tail, parts that fit the parts region, no
+    // bias (each part would add it)
+    const int num_n = args.N / bn, num_tiles = ((args.M + BM - 1) / BM) * num_n;
+    if (bn != kGemmBN || !m.out2 || args.bias || args.splits < 1 || args.splits > args.K / BK ||
+        args.main_tiles < 0 || args.main_tiles >= num_tiles || args.main_tiles % num_n ||
+        args.tail_row0 != (args.main_tiles / num_n) * BM || args.split_rows % BM ||
+        args.split_rows < ((args.M - args.tail_row0 + BM - 1) / BM) * BM)
+      return cudaErrorInvalidValue;
+  }
   if (bn == kGemmBNNarrow) {
     // narrow tiles: the residual GEMMs with N = 1024 (more tiles per wave)
     if (epilogue == kEpiResid) return launch_one<kEpiResid, kGemmBNNarrow>(m, args, num_sms, stream);
@@ -606,6 +666,7 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
     case kEpiScorer: return launch_one<kEpiScorer, kGemmBN>(m, args, num_sms, stream);
     case kEpiStoreF32: return launch_one<kEpiStoreF32, kGemmBN>(m, args, num_sms, stream);
     case kEpiPartial: return launch_one<kEpiPartial, kGemmBN>(m, args, num_sms, stream);
+    case kEpiResidTail: return launch_one<kEpiResidTail, kGemmBN>(m, args, num_sms, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -38,6 +38,13 @@ enum GemmEpilogue : int {
   // kernel adds the parts to the residual in part order (deterministic), so
   // small-M GEMMs spread their K loop over more SMs.
   kEpiPartial = 7,
+  // residual GEMM whose tiles do not fill the last wave: work units below
+  // main_tiles are whole tiles reduce-added into x (kEpiResid, no bias);
+  // the remaining tiles (whole row blocks from tail_row0 on) are cut into
+  // `splits` K parts each, and part s of a tile stores its f32 sum at rows
+  // s * split_rows + (row - tail_row0) of the second output map (the parts
+  // region), for the next LayerNorm to add in part order
+  kEpiResidTail = 8,
 };
 
 struct GemmArgs {
@@ -54,8 +61,11 @@ struct GemmArgs {
   float scale;         // q/k scale
   const float* wvec;   // scorer output weights [N]
   int n_valid;         // valid output columns for kEpiGeglu
-  int splits;          // kEpiPartial: K parts (>= 1)
-  int split_rows;      // kEpiPartial: output rows per part (multiple of 256, >= M)
+  int splits;          // kEpiPartial / kEpiResidTail: K parts (>= 1)
+  int split_rows;      // kEpiPartial: output rows per part (multiple of 256, >= M);
+                       // kEpiResidTail: the same for the tail rows (>= M - tail_row0)
+  int main_tiles;      // kEpiResidTail: tiles reduce-added whole (a multiple of N / 256)
+  int tail_row0;       // kEpiResidTail: first row of the split tiles (main_tiles / (N / 256) * 256)
   unsigned long long wait_limit_ns;  // 0: the default bound (2 s)
   int stuck;           // timeout test: the producers first wait on a barrier nothing completes
 };
@@ -76,6 +86,7 @@ struct GemmMaps {
   const CUtensorMap* a;
   const CUtensorMap* b;
   const CUtensorMap* out;
+  const CUtensorMap* out2 = nullptr;  // kEpiResidTail: the parts region
 };
 
 // bn: kGemmBN, or kGemmBNNarrow for kEpiResid / kEpiStoreF32 (then the
@@ -132,12 +143,14 @@ cudaError_t launch_ln(const float* x, const int* idx, const float* w, const floa
                       __half* t16, int rows, cudaStream_t s);
 // x[r] = t16[r] = LN(x[r]) * w  (each warp reads its row before writing it)
 cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, int rows, cudaStream_t s);
-// Split-K partial sums waiting to be added to the residual stream: part s of
-// row r is parts[s * stride + r * 1024 + c], s < nparts.
+// Split-K partial sums waiting to be added to the residual stream: rows r >=
+// row0 have them, part s of row r at parts[s * stride + (r - row0) * 1024 +
+// c], s < nparts; rows below row0 have none.
 struct PendingParts {
   const float* parts = nullptr;
   int nparts = 0;
   size_t stride = 0;
+  int row0 = 0;
 };
 // x[r] += sum_s parts[s][r] (parts summed in order, then added);
 // t16[r] = LN(x[r]) * w (+ b)

@@ -107,7 +107,8 @@ __device__ __forceinline__ void scale_shift(float (&v)[32], int lane, const floa
 // first (so the result does not depend on which CTA finished first).  The
 // parts are read once: streaming loads.
 __device__ __forceinline__ void add_parts(float (&v)[32], const PendingParts& p, size_t row, int lane) {
-  if (p.nparts <= 0) return;
+  if (p.nparts <= 0 || row < static_cast<size_t>(p.row0)) return;
+  row -= static_cast<size_t>(p.row0);
   float ps[32];
   const float4* q = reinterpret_cast<const float4*>(p.parts + row * HID);
 #pragma unroll
@@ -168,10 +169,12 @@ __device__ __forceinline__ float4 ld_stream_f4(const float4* p) {
 }
 
 // add_parts with the part count known at compile time: the loads of G
-// float4 chunks of every part are issued together (32 loads in flight per
-// lane), then summed in add_parts' order, element by element.
+// float4 chunks of every part are issued together (G * NP loads in flight
+// per lane), then summed in add_parts' order, element by element.  The
+// caller skips rows below p.row0 (they have no parts).
 template <int NP>
 __device__ __forceinline__ void add_parts_static(float (&v)[32], const PendingParts& p, size_t row, int lane) {
+  row -= static_cast<size_t>(p.row0);
   constexpr int G = 32 / NP >= 8 ? 8 : 32 / NP;
   const float4* q = reinterpret_cast<const float4*>(p.parts + row * HID);
   const size_t st4 = p.stride / 4;
@@ -198,20 +201,25 @@ __device__ __forceinline__ void add_parts_static(float (&v)[32], const PendingPa
 }
 
 // The residual add of a split-K GEMM (x += its NP parts) fused with the
-// LayerNorm that follows it.
+// LayerNorm that follows it.  Rows below p.row0 have no parts: they are only
+// normalised (their residual row is not rewritten).
 template <int NP>
 __global__ void __launch_bounds__(256) ln_parts_kernel(float* x, const PendingParts p, const float* w,
                                                        const float* b, float eps, __half* t16, int rows) {
   grid_dep_wait();
   grid_dep_trigger();
-  const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
+  // CTAs in reverse row order: the rows with parts (the last ones) read the
+  // most and start first
+  const int row = (gridDim.x - 1 - blockIdx.x) * ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float* xr = x + static_cast<size_t>(row) * HID;
   float v[32];
   load_f32(xr, lane, v);
-  add_parts_static<NP>(v, p, static_cast<size_t>(row), lane);
-  store_f32(xr, lane, v);
+  if (row >= p.row0) {
+    add_parts_static<NP>(v, p, static_cast<size_t>(row), lane);
+    store_f32(xr, lane, v);
+  }
   normalize(v, eps);
   scale_shift(v, lane, w, b);
   store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
@@ -225,7 +233,7 @@ __global__ void __launch_bounds__(256) add_parts_kernel(float* x, const PendingP
   grid_dep_trigger();
   const int row = blockIdx.x * ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  if (row >= rows || row < p.row0) return;  // rows below row0 have no parts
   float* xr = x + static_cast<size_t>(row) * HID;
   float v[32];
   load_f32(xr, lane, v);
@@ -291,7 +299,7 @@ cudaError_t launch_ln_parts_n(float* x, const PendingParts& p, const float* w, c
 cudaError_t launch_ln_parts(float* x, const PendingParts& p, const float* w, const float* b, float eps,
                             __half* t16, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID || p.stride % 4)
+  if (!p.parts || p.nparts < 1 || p.row0 < 0 || p.stride < static_cast<size_t>(rows - p.row0) * HID || p.stride % 4)
     return cudaErrorInvalidValue;
   switch (p.nparts) {
     case 1: return launch_ln_parts_n<1>(x, p, w, b, eps, t16, rows, s);
@@ -308,7 +316,8 @@ cudaError_t launch_ln_parts(float* x, const PendingParts& p, const float* w, con
 
 cudaError_t launch_add_parts(float* x, const PendingParts& p, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
-  if (!p.parts || p.nparts < 1 || p.stride < static_cast<size_t>(rows) * HID) return cudaErrorInvalidValue;
+  if (!p.parts || p.nparts < 1 || p.row0 < 0 || p.stride < static_cast<size_t>(rows - p.row0) * HID)
+    return cudaErrorInvalidValue;
   return launch_pdl(add_parts_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, rows);
 }
 
@@ -316,7 +325,8 @@ cudaError_t launch_final_ln(float* x, const float* wf, const __half* type_emb, c
                             const float* w1, const float* b1, float eps, __half* t16, int rows,
                             cudaStream_t s, const PendingParts& p) {
   if (rows <= 0) return cudaSuccess;
-  if (p.nparts > 0 && (!p.parts || p.stride < static_cast<size_t>(rows) * HID)) return cudaErrorInvalidValue;
+  if (p.nparts > 0 && (!p.parts || p.row0 < 0 || p.stride < static_cast<size_t>(rows - p.row0) * HID))
+    return cudaErrorInvalidValue;
   return launch_pdl(final_ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, wf, type_emb, rowtype,
                     w1, b1, eps, t16, rows, p);
 }

@@ -57,6 +57,7 @@ def lib():
         L.laya_open_empty.argtypes = [ctypes.c_int, ctypes.POINTER(vp)]
         L.laya_upload_weight_f16.argtypes = [vp, ctypes.c_char_p, ctypes.c_void_p, _i64p, ctypes.c_int]
         L.laya_upload_weight_f32.argtypes = [vp, ctypes.c_char_p, _f32p, _i64p, ctypes.c_int]
+        L.laya_upload_weight_f32_graph.argtypes = [vp, ctypes.c_char_p, _f32p, _i64p, ctypes.c_int]
         L.laya_finalize.argtypes = [vp]
         L.laya_forward.argtypes = [vp, ctypes.POINTER(_CReq), _f32p, _f32p]
         L.laya_forward_tapped.argtypes = [vp, ctypes.POINTER(_CReq), _f32p, _f32p, TAP_FN, vp]
@@ -223,6 +224,13 @@ class Engine:
         dims = np.asarray(a.shape, dtype=np.int64)
         _check(lib().laya_upload_weight_f32(self._h, name.encode(), a.ctypes.data_as(_f32p),
                                             dims.ctypes.data_as(_i64p), a.ndim))
+
+    def upload_f32_graph(self, name: str, data: np.ndarray) -> None:
+        """A tensor in graph layout (Tensors::f32 / Tensors::dims, weights.rs:270-295)."""
+        a = np.ascontiguousarray(data, dtype=np.float32)
+        dims = np.asarray(a.shape, dtype=np.int64)
+        _check(lib().laya_upload_weight_f32_graph(self._h, name.encode(), a.ctypes.data_as(_f32p),
+                                                  dims.ctypes.data_as(_i64p), a.ndim))
 
     def finalize(self) -> None:
         _check(lib().laya_finalize(self._h))
