@@ -80,6 +80,9 @@ def parse():
     ap.add_argument("--stream-window", type=int, default=0,
                     help="stream: group questions by length within windows of this many consecutive "
                          "requests (0, the default: pack in dispatch order)")
+    ap.add_argument("--stream-requests", type=int, default=1024,
+                    help="forward-16k: requests of the request-stream sweep carried in the line's `stream` key "
+                         "(0: none)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
 
@@ -482,6 +485,9 @@ def run_forward(args, d, eng):
            "latency_ms": latency_summary(e_ms),
            "path": "laya_forward (validate + compact on host, one pinned H2D, graph-free launch, D2H)"}
 
+    # every rank: the bounded request-stream sweep (collective steps inside)
+    stream_info = stream_key(args, d, eng) if args.config == "forward-16k" else None
+
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         sample = sub_request(req, args.cpu_sample)
@@ -506,7 +512,7 @@ def run_forward(args, d, eng):
                                    "launches_per_step": gemm_launches // args.steps,
                                    "flops_per_step": workloads.gemm_flops(req)},
                          kernels=kernels, e2e=e2e, gpu_launches=launches * args.steps, clocks=clk,
-                         cpu_baseline=cpu, parity=parity)
+                         cpu_baseline=cpu, parity=parity, stream=stream_info)
         print(json.dumps(line), flush=True)
     plan.close()
 
@@ -763,19 +769,22 @@ def run_request(args, d, eng):
     tok.close()
 
 
-def run_stream(args, d, eng):
-    """Config 4: the request stream (JSON) through the C++ front end: every
-    rank plans all requests on its host threads to learn their token costs,
-    takes the share the greedy cost assignment gives it, and packs its
-    questions across requests into <=16384-token forwards in dispatch order
-    (with --stream-window W: grouped by length within windows of W
-    consecutive requests; measured 2.4% more tokens/s for 2.8x the median
-    service latency at W = 64, so not the default)."""
-    import numpy as np
+def stream_pass(args, d, eng, n_requests, window, warmup):
+    """One pass over the first `n_requests` requests of the request stream
+    (configuration 4, JSON) through the C++ front end: every rank plans all
+    of them on its host threads to learn their token costs, takes the share
+    the greedy cost assignment gives it, and packs its questions across
+    requests into <=16384-token forwards in dispatch order (window W > 0:
+    grouped by length within windows of W consecutive requests; measured
+    2.4% more tokens/s for 2.8x the median service latency at W = 64, so not
+    the default).  The forwards run once device-resident (plans, CUDA events,
+    max over ranks), then once through the public call with scoring and
+    response JSON (wall clock).  Every rank takes the same collective steps;
+    the returned figures are whole-job aggregates."""
     from laya_rust_b200 import frontend as FE, modelgen, workloads
     torch = d.torch
     tok = FE.Tokenizer(gguf_path=modelgen.cached_model(seed=0))
-    texts = [json.dumps(r) for r in workloads.request_stream_json(request_words(), args.requests, 4)]
+    texts = [json.dumps(r) for r in workloads.request_stream_json(request_words(), n_requests, 4)]
     t = time.perf_counter()
     allq = FE.Requests(tok, texts, threads=0)
     plan_all_s = time.perf_counter() - t
@@ -784,17 +793,11 @@ def run_stream(args, d, eng):
         r, ln, _, _ = allq.question_shape(i)
         cost[r] += ln
     allq.close()
-    load = [0] * d.world
-    mine = []
-    for r, c in enumerate(cost):   # greedy by token cost, in dispatch order
-        g = min(range(d.world), key=lambda w: (load[w], w))
-        load[g] += c
-        if g == d.rank:
-            mine.append(r)
+    mine = workloads.assign_by_cost(cost, d.world)[d.rank]   # greedy by token cost, in dispatch order
     t = time.perf_counter()
     rq = FE.Requests(tok, [texts[i] for i in mine], threads=0)
     plan_s = time.perf_counter() - t
-    nf = rq.pack_windows(16384, args.stream_window) if args.stream_window > 0 else rq.pack(16384, True)
+    nf = rq.pack_windows(16384, window) if window > 0 else rq.pack(16384, True)
     batches = [rq.batch(f) for f in range(nf)]
     fq = [rq.forward_questions(f) for f in range(nf)]
     q_req = [rq.question_shape(i)[0] for i in range(rq.questions())]
@@ -809,8 +812,8 @@ def run_stream(args, d, eng):
     # the first W
     idx = range(len(plans))
     big = {max(idx, key=lambda i: plans[i].stats()[0]), max(idx, key=lambda i: batches[i].n * batches[i].k),
-           max(idx, key=lambda i: batches[i].n), max(idx, key=lambda i: batches[i].l)}
-    for i in sorted(big) + list(range(min(args.warmup, len(plans)))):
+           max(idx, key=lambda i: batches[i].n), max(idx, key=lambda i: batches[i].l)} if plans else set()
+    for i in sorted(big) + list(range(min(warmup, len(plans)))):
         plans[i].run()
     torch.cuda.synchronize()
     clocks = ClockSampler(list(range(d.world))) if d.rank == 0 else None
@@ -857,11 +860,27 @@ def run_stream(args, d, eng):
     all_completion = [v for part in d.gather(completion) for v in part]
     total_real = d.allsum(real)
     forwards = d.allsum(nf)
-    plan_tokens = d.allsum(real)
     plan_s_max = d.allmax(plan_s)
     questions_all = d.allsum(rq.questions())   # every rank takes the same collective steps
     padded_all = d.allsum(padded)
+    gpus_active = d.allsum(1 if nf > 0 else 0)
+    res = {"requests": len(texts), "questions": int(questions_all), "forwards": int(forwards),
+           "real_tokens": int(total_real), "ms_max": ms_max, "value": total_real / (ms_max / 1e3),
+           "padded_tokens_per_s": padded_all / (ms_max / 1e3), "e2e_s": e_sec, "e2e_value": total_real / e_sec,
+           "service_latency_ms": latency_summary(all_service),
+           "completion_latency_ms": latency_summary(all_completion), "gpus_active": int(gpus_active),
+           "launches": launches, "upload": upload, "plan_s_max": plan_s_max, "plan_all_s": plan_all_s,
+           "nf": nf, "d2h": sum(4 * (b.n * b.k + 2 * b.n) for b in batches), "clocks": clk,
+           "warmup": min(warmup, len(plans)) + len(big)}
+    rq.close()
+    tok.close()
+    return res
 
+
+def run_stream(args, d, eng):
+    """Config 4: the request stream (JSON) through the C++ front end, one
+    pass over --requests requests (stream_pass)."""
+    res = stream_pass(args, d, eng, args.requests, args.stream_window, args.warmup)
     cpu = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu_baseline:
         ct, toks = cpu_request_run([stream_sample()], 1, 0)
@@ -869,30 +888,48 @@ def run_stream(args, d, eng):
                                 f"request 0 with its first 4 questions ({toks} tokens) through run_all "
                                 "(restated front end + C oracle forward), one run")
     if d.rank == 0:
-        cfg = {"workload": "stream", "model": MODEL, "requests": len(texts), "questions": int(questions_all),
-               "forwards": int(forwards), "real_tokens": int(total_real), "max_tokens_per_forward": 16384,
+        cfg = {"workload": "stream", "model": MODEL, "requests": res["requests"], "questions": res["questions"],
+               "forwards": res["forwards"], "real_tokens": res["real_tokens"], "max_tokens_per_forward": 16384,
                "packing": (f"group_by_budget within windows of {args.stream_window} requests"
                            if args.stream_window > 0 else "dispatch order"),
                "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
                "l2": "working set > L2 (843 MB f16 weights streamed per forward)"}
-        steps = nf
-        e2e = {"value": total_real / e_sec, "unit": UNIT, "h2d_bytes_per_step": upload / steps,
-               "d2h_bytes_per_step": sum(4 * (b.n * b.k + 2 * b.n) for b in batches) / steps,
-               "makespan_s": e_sec, "service_latency_ms": latency_summary(all_service),
-               "completion_latency_ms": latency_summary(all_completion),
+        steps = res["nf"]
+        e2e = {"value": res["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": res["upload"] / steps,
+               "d2h_bytes_per_step": res["d2h"] / steps,
+               "makespan_s": res["e2e_s"], "service_latency_ms": res["service_latency_ms"],
+               "completion_latency_ms": res["completion_latency_ms"],
                "path": "laya_forward per packed forward, C++ scoring and response JSON"}
-        frontend = {"plan_s": plan_s_max, "plan_tokens_per_s": plan_tokens / plan_s_max,
-                    "plan_all_requests_s": plan_all_s, "host_threads": os.cpu_count(),
+        frontend = {"plan_s": res["plan_s_max"], "plan_tokens_per_s": res["real_tokens"] / res["plan_s_max"],
+                    "plan_all_requests_s": res["plan_all_s"], "host_threads": os.cpu_count(),
                     "what": "parse + tokenize + System One layout of the rank's requests on all host threads"}
-        line = base_line(args, METRIC + " (request stream)", total_real / (ms_max / 1e3), UNIT, d.world,
-                         ms_max / steps, cfg, padded_tokens_per_s=padded_all / (ms_max / 1e3),
-                         device_makespan_s=ms_max / 1e3, e2e=e2e, frontend=frontend, gpu_launches=launches,
-                         clocks=clk, cpu_baseline=cpu)
+        line = base_line(args, METRIC + " (request stream)", res["value"], UNIT, d.world,
+                         res["ms_max"] / steps, cfg, padded_tokens_per_s=res["padded_tokens_per_s"],
+                         device_makespan_s=res["ms_max"] / 1e3, e2e=e2e, frontend=frontend,
+                         gpus_active=res["gpus_active"], gpu_launches=res["launches"], clocks=res["clocks"],
+                         cpu_baseline=cpu)
         line["steps"] = steps
-        line["warmup"] = min(args.warmup, len(plans)) + len(big)
+        line["warmup"] = res["warmup"]
         print(json.dumps(line), flush=True)
-    rq.close()
-    tok.close()
+
+
+def stream_key(args, d, eng):
+    """The bounded request-stream sweep carried by the forward-16k line (the
+    one the 1/2/4/8-GPU scaling run records): the first --stream-requests
+    requests of configuration 4, sharded over the ranks by token cost."""
+    if args.stream_requests <= 0:
+        return None
+    res = stream_pass(args, d, eng, args.stream_requests, 0, 2)
+    svc, cmp_ = res["service_latency_ms"], res["completion_latency_ms"]
+    return {"requests": res["requests"], "questions": res["questions"], "forwards": res["forwards"],
+            "real_tokens": res["real_tokens"], "value": res["value"], "unit": UNIT,
+            "device_makespan_s": res["ms_max"] / 1e3, "e2e_value": res["e2e_value"], "e2e_makespan_s": res["e2e_s"],
+            "service_latency_ms": {"p50": svc["p50"], "p99": svc["p99"]},
+            "completion_latency_ms": {"p50": cmp_["p50"], "p99": cmp_["p99"]},
+            "gpus_active": res["gpus_active"],
+            "parallelism": f"request-dp{d.world} (greedy by token cost, no collective)",
+            "what": "configuration 4's first requests: value = real tokens / device makespan (max over ranks); "
+                    "e2e_value through laya_forward + scoring + response JSON (wall clock, max over ranks)"}
 
 
 def run_b200(args):

@@ -1,5 +1,6 @@
 // Attention for sequences of at most 128 tokens on the 5th-generation tensor
-// cores: one CTA per (tile, head), a single pass.
+// cores: a persistent, warp-specialised kernel that keeps four (tile, head)
+// units in flight per SM.
 //
 // Contract (laya-rust backend/cpu/mod.rs:257-314 with the masks of
 // :316-328): out = softmax(q . k^T + mask) . v per (sequence, head), q and k
@@ -9,23 +10,38 @@
 // A tile packs whole consecutive sequences of at most 128 tokens (adjacent
 // in the compacted rows) into at most 128 rows; each row sees only its own
 // sequence's keys, so packing changes no result and the tiles carry few
-// padding rows.  Per CTA (128 threads, 48 KB shared memory, 128 TMEM
-// columns: four CTAs per SM):
-//   TMA      Q, K, V [128 rows x 64] of one head from the token-major qkv
-//            buffer, 128-byte swizzle
-//   MMA 1    S = Q . K^T -> TMEM columns [0, 128)     (M=128, N=128, K=64)
-//   softmax  thread t owns query row t = TMEM lane t: its visible keys are an
-//            interval; it streams its scores from TMEM 32 keys at a time
-//            (chunks no row of the warp sees are skipped, chunks every row of
-//            the warp sees fully take a path without selects), takes the
-//            maximum, then writes P = exp(s - max) as f16 into shared memory
-//            over the dead Q and K tiles (the swizzled K-major operand layout)
-//            and sums it
-//   MMA 2    O = P . V -> TMEM columns [0, 64) over the dead S (M=128, N=64,
-//            K=128), V as an MN-major operand
-//   store    thread t scales its O row by 1 / sum and writes 64 f16
-// Every wait is bounded; a CTA whose wait expires records the error, lets
-// the operations it issued land and returns.
+// padding rows.  A unit is (tile, head); unit u of the launch is tile u / 16,
+// head u % 16, and CTA c (one per SM) takes units c, c + gridDim.x, ...
+//
+// Each CTA has four slots.  Slot s holds its units k = s, s + 4, ... (k
+// counts this CTA's units): a shared-memory stage (Q | K | V, 16 KB each,
+// 128-byte swizzle, only the 32-row boxes the tile's rows need) and 128 TMEM
+// columns (S, then O over it).  Roles (576 threads):
+//   warp 0      TMA producer: loads unit k into slot k % 4 as soon as the P.V
+//               of unit k - 4 has completed (the stage is free)
+//   warp 1      TMEM allocation; one thread issues the MMAs in unit order,
+//               S(k) and P.V(k) each as soon as its inputs are ready (a
+//               non-blocking poll over the two next steps):
+//                 S = Q . K^T        (M=128, N=128, K=64) into the slot's TMEM
+//                 O = P . V          (M=128, N=64, K=128) over the dead S
+//   warps 2-17  four softmax warpgroups, warpgroup s serving slot s: thread t
+//               owns query row t = TMEM lane t.  Its visible keys are an
+//               interval; it streams its scores from TMEM 32 keys at a time
+//               (chunks no row of the warp sees are skipped, chunks every row
+//               of the warp sees fully take a path without selects), takes
+//               the maximum, writes P = 2^(s log2 e - max) as f16 into the
+//               slot's dead Q and K tiles (the swizzled K-major operand
+//               layout) and sums it; after P.V it scales its O row by 1 / sum
+//               and stores 64 f16 outputs, then frees the slot's TMEM.
+// So one slot's loads, another's MMAs and the softmax of the other two run
+// at the same time, and no unit waits for a launch.
+// Rows a tile does not use are never loaded: K rows past them are stale
+// (their scores are masked), V rows past them hold an earlier unit's finite
+// values or the zeros written at start (P is 0 there).
+// Every wait is bounded; on expiry the thread records the error and raises
+// the CTA's abort flag, every role leaves its loop, the MMA thread waits
+// (bounded) for the MMAs it issued, the CTA lingers 2 ms so loads in flight
+// land, and TMEM is freed.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -35,10 +51,19 @@ namespace {
 
 constexpr int TQ = 128;
 constexpr int D = 64;
-constexpr int THREADS = 128;
-constexpr int TILE_BYTES = TQ * D * 2;  // 16 KB: one [128 x 64] f16 tile
-constexpr int TMEM_COLS = 128;
-constexpr size_t SMEM = 1024 + 3 * TILE_BYTES + 64;  // + barriers kv, s, o, stuck, drain and the TMEM address
+constexpr int BOX = kAttnTcBoxRows;         // 32 rows per TMA box
+constexpr int NSLOT = 4;
+constexpr int SOFTMAX_WARPS = 4 * NSLOT;
+constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;
+constexpr int TILE_BYTES = TQ * D * 2;      // 16 KB: one [128 x 64] f16 tile
+constexpr int BOX_BYTES = BOX * D * 2;      // 4 KB
+constexpr int STAGE_BYTES = 3 * TILE_BYTES; // Q | K | V
+constexpr int OFF_BAR = NSLOT * STAGE_BYTES;
+// barriers per slot: kv_full, s_full, p_full, o_full, tmem_free; then drain,
+// stuck, the TMEM address and the abort flag
+constexpr int NBARS = 5 * NSLOT + 2;
+constexpr size_t SMEM = 1024 + OFF_BAR + NBARS * 8 + 16;
+constexpr int TMEM_COLS = 512;              // slot s at column s * 128
 constexpr float L2E = 1.4426950408889634f;
 
 constexpr uint32_t IDESC_QK = umma_idesc_f16(TQ, TQ);
@@ -69,6 +94,19 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Non-blocking test of a barrier phase.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Bits j of a 32-key chunk with a <= j < b (relative to the chunk).
 __device__ __forceinline__ uint32_t chunk_mask(int a, int b) {
   const int lo = a < 0 ? 0 : (a > 32 ? 32 : a);
@@ -78,190 +116,288 @@ __device__ __forceinline__ uint32_t chunk_mask(int a, int b) {
   return static_cast<uint32_t>(m);
 }
 
-__global__ void __launch_bounds__(THREADS, 4)
+// Lane 0 waits (bounded) and the warp agrees on the outcome; a warp that
+// already failed does not wait again.
+__device__ __forceinline__ bool warp_wait(bool ok, uint64_t* bar, uint32_t parity, const AttnShortArgs& a,
+                                          volatile int* abort_flag) {
+  int w = ok ? 1 : 0;
+  if (ok && (threadIdx.x & 31) == 0)
+    w = mbar_wait_bounded(bar, parity, a.err, kErrAttnWait, abort_flag, a.wait_limit_ns);
+  return __shfl_sync(0xffffffffu, w, 0) != 0;
+}
+
+__device__ __forceinline__ int boxes_of(int rows) { return rows <= 0 ? 1 : (rows + BOX - 1) / BOX; }
+
+__global__ void __launch_bounds__(THREADS, 1)
     attn_short_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ AttnShortArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint8_t* sQ = smem;                   // then P, over Q and K
-  uint8_t* sK = smem + TILE_BYTES;
-  uint8_t* sV = smem + 2 * TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + 3 * TILE_BYTES);
-  uint64_t* kv_bar = bars;
-  uint64_t* s_bar = bars + 1;
-  uint64_t* o_bar = bars + 2;
-  uint64_t* stuck_bar = bars + 3;  // nothing ever arrives on it (the timeout test)
-  uint64_t* drain = bars + 4;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 5);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* s_full = kv_full + NSLOT;
+  uint64_t* p_full = s_full + NSLOT;
+  uint64_t* o_full = p_full + NSLOT;
+  uint64_t* tmem_free = o_full + NSLOT;
+  uint64_t* drain = tmem_free + NSLOT;
+  uint64_t* stuck_bar = drain + 1;  // nothing ever arrives on it (the timeout test)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(stuck_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int2 tile = a.tiles[blockIdx.x];  // (first row, rows); uploaded before every kernel of the forward
-  const int h = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int total_units = a.num_tiles * 16;
+  const int my_units = static_cast<int>(blockIdx.x) < total_units
+                           ? (total_units - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1
+                           : 0;
+
   if (tid == 0) {
-    for (int i = 0; i < 5; ++i) mbar_init(&bars[i], 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 4);     // the four warps of the slot's warpgroup
+      mbar_init(&o_full[s], 1);
+      mbar_init(&tmem_free[s], 4);
+    }
+    mbar_init(drain, 1);
+    mbar_init(stuck_bar, 1);
+    *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tm_qkv);
   }
-  if (warp == 0) {
+  // V rows never loaded must be finite: zeros until a unit overwrites them
+  {
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    for (int i = tid; i < NSLOT * TILE_BYTES / 16; i += THREADS) {
+      const int s = i / (TILE_BYTES / 16), j = i - s * (TILE_BYTES / 16);
+      reinterpret_cast<uint4*>(smem + s * STAGE_BYTES + 2 * TILE_BYTES)[j] = z;
+    }
+  }
+  if (warp == 1) {
     tmem_alloc(tmem_holder, TMEM_COLS);
     tmem_relinquish();
   }
+  fence_proxy_async_smem();  // the zeros, before the tensor core reads them
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_holder;
+  // the tiles come from the plan upload, which precedes every kernel of the
+  // forward; q/k/v are written by the previous kernel
   grid_dep_wait();
   grid_dep_trigger();
 
-  bool ok = true;
-  if (tid == 0) {
-    if (a.stuck) ok = mbar_wait_bounded(stuck_bar, 0, a.err, kErrAttnWait, nullptr, a.wait_limit_ns);
-    if (ok) {
-      const uint64_t pol = l2_evict_first();
-      mbar_arrive_expect_tx(kv_bar, 3 * TILE_BYTES);
-      tma_load_2d_hint(sQ, &tm_qkv, h * D, tile.x, kv_bar, pol);
-      tma_load_2d_hint(sK, &tm_qkv, 1024 + h * D, tile.x, kv_bar, pol);
-      tma_load_2d_hint(sV, &tm_qkv, 2048 + h * D, tile.x, kv_bar, pol);
-    }
-  }
-  // the query row of this thread and its visible keys (tile-relative)
-  const int r = tid;
-  int lo = 0, hi = 0;
-  if (r < tile.y) {
-    const int s = a.rowseq[tile.x + r];
-    const int st = a.seq_start[s] - tile.x, en = st + a.seq_len[s];
-    lo = a.window >= 0 && r - a.window > st ? r - a.window : st;
-    hi = a.window >= 0 && r + a.window + 1 < en ? r + a.window + 1 : en;
-  }
-  if (__syncthreads_or(!ok)) ok = false;
-  if (ok) ok = mbar_wait_bounded(kv_bar, 0, a.err, kErrAttnWait, nullptr, a.wait_limit_ns);
-  if (__syncthreads_or(!ok)) ok = false;
-
-  // S = Q . K^T
-  if (ok && tid == 0) {
-    tc_fence_after();
-    const uint64_t dq = umma_desc_sw128(smem_u32(sQ)), dk = umma_desc_sw128(smem_u32(sK));
-#pragma unroll
-    for (int k = 0; k < D / 16; ++k)
-      umma_f16(tmem, dq + static_cast<uint64_t>(2 * k), dk + static_cast<uint64_t>(2 * k), IDESC_QK, k > 0);
-    umma_commit(s_bar);
-  }
-  if (ok) ok = mbar_wait_bounded(s_bar, 0, a.err, kErrAttnWait, nullptr, a.wait_limit_ns);
-  if (__syncthreads_or(!ok)) ok = false;
-
-  const uint32_t t_row = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  float sum = 0.0f;
-  if (ok) {
-    tc_fence_after();
-    uint32_t mask[4];
-    bool any[4], all[4];
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      mask[ch] = chunk_mask(lo - 32 * ch, hi - 32 * ch);
-      any[ch] = __any_sync(0xffffffffu, mask[ch] != 0u);
-      all[ch] = __all_sync(0xffffffffu, mask[ch] == 0xffffffffu);
-    }
-    float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      if (!any[ch]) continue;
-      uint32_t v[32];
-      tmem_ld_32x32b_x32(t_row + 32 * ch, v);
-      tmem_ld_wait();
-      if (all[ch]) {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], u2f(v[j]));
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], (mask[ch] >> j) & 1u ? u2f(v[j]) : -INFINITY);
+  if (warp == 0) {
+    // ---- TMA producer -------------------------------------------------------------
+    if (lane == 0) {
+      bool ok = true;
+      if (a.stuck) ok = mbar_wait_bounded(stuck_bar, 0, a.err, kErrAttnWait, abort_flag, a.wait_limit_ns);
+      const uint64_t pol = l2_evict_first();  // q/k/v are read by this launch only
+      for (int k = 0; k < my_units && ok; ++k) {
+        const int s = k % NSLOT, j = k / NSLOT;
+        if (j > 0 && !(ok = mbar_wait_bounded(&o_full[s], (j - 1) & 1, a.err, kErrAttnWait, abort_flag,
+                                              a.wait_limit_ns)))
+          break;
+        const int u = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        const int2 tile = __ldg(a.tiles + (u >> 4));
+        const int h = u & 15;
+        const int nb = boxes_of(tile.y);
+        uint8_t* st = smem + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[s], 3 * nb * BOX_BYTES);
+        for (int b = 0; b < nb; ++b) {
+          tma_load_2d_hint(st + b * BOX_BYTES, &tm_qkv, h * D, tile.x + b * BOX, &kv_full[s], pol);
+          tma_load_2d_hint(st + TILE_BYTES + b * BOX_BYTES, &tm_qkv, 1024 + h * D, tile.x + b * BOX, &kv_full[s],
+                           pol);
+          tma_load_2d_hint(st + 2 * TILE_BYTES + b * BOX_BYTES, &tm_qkv, 2048 + h * D, tile.x + b * BOX,
+                           &kv_full[s], pol);
+        }
       }
+      if (!ok) *abort_flag = 1;
     }
-    const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-    const float ms = (m == -INFINITY ? 0.0f : m) * L2E;
-    float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  } else if (warp == 1) {
+    // ---- MMA issuer: S(k) and P.V(k) in unit order, each when ready ------------
+    if (lane == 0) {
+      int ks = 0, kp = 0;  // next unit for S, next for P.V
+      const unsigned long long limit = a.wait_limit_ns ? a.wait_limit_ns : kWaitLimitNs;
+      unsigned long long t0 = global_ns();
+      uint32_t idle = 0;
+      while (kp < my_units) {
+        bool progressed = false;
+        if (ks < my_units && ks - kp < NSLOT) {
+          const int s = ks % NSLOT, j = ks / NSLOT;
+          if (mbar_test(&kv_full[s], j & 1) && (j == 0 || mbar_test(&tmem_free[s], (j - 1) & 1))) {
+            tc_fence_after();
+            uint8_t* st = smem + s * STAGE_BYTES;
+            const uint64_t dq = umma_desc_sw128(smem_u32(st)), dk = umma_desc_sw128(smem_u32(st + TILE_BYTES));
+            const uint32_t d_tmem = tmem + static_cast<uint32_t>(s * 128);
 #pragma unroll
-    for (int ch = 0; ch < 4; ++ch) {
-      uint32_t w[16];
-      if (!any[ch]) {
+            for (int kk = 0; kk < D / 16; ++kk)
+              umma_f16(d_tmem, dq + static_cast<uint64_t>(2 * kk), dk + static_cast<uint64_t>(2 * kk), IDESC_QK,
+                       kk > 0);
+            umma_commit(&s_full[s]);
+            ++ks;
+            progressed = true;
+          }
+        }
+        if (kp < ks) {
+          const int s = kp % NSLOT, j = kp / NSLOT;
+          if (mbar_test(&p_full[s], j & 1)) {
+            tc_fence_after();
+            uint8_t* st = smem + s * STAGE_BYTES;
+            const uint64_t dp = umma_desc_sw128(smem_u32(st));
+            const uint64_t dv = desc_mn_sw128(smem_u32(st + 2 * TILE_BYTES));
+            const uint32_t d_tmem = tmem + static_cast<uint32_t>(s * 128);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) w[j] = 0u;
-      } else {
+            for (int kk = 0; kk < TQ / 16; ++kk)
+              umma_f16(d_tmem, dp + static_cast<uint64_t>((kk >> 2) * (TILE_BYTES >> 4) + (kk & 3) * 2),
+                       dv + static_cast<uint64_t>(kk * (2048 >> 4)), IDESC_PV, kk > 0);
+            umma_commit(&o_full[s]);
+            ++kp;
+            progressed = true;
+          }
+        }
+        if (progressed) {
+          t0 = global_ns();
+          idle = 0;
+        } else {
+          if (*abort_flag) break;
+          if ((++idle & 63u) == 0) {
+            if (global_ns() - t0 > limit) {
+              atomicCAS(a.err, 0, kErrAttnWait);
+              *abort_flag = 1;
+              break;
+            }
+            __nanosleep(64);
+          }
+        }
+      }
+      // every MMA issued here completes before TMEM is released
+      umma_commit(drain);
+      mbar_wait_bounded(drain, 0, a.err, kErrAttnWait, nullptr);
+    }
+  } else {
+    // ---- softmax warpgroup s ------------------------------------------------------
+    const int s = (warp - 2) >> 2;
+    const int q = warp & 3;        // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;   // query row within the tile
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(s * 128);
+    uint8_t* st = smem + s * STAGE_BYTES;
+    bool ok = true;
+    for (int k = s, j = 0; k < my_units && ok; k += NSLOT, ++j) {
+      const int u = static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+      const int2 tile = __ldg(a.tiles + (u >> 4));
+      const int h = u & 15;
+      // the query row's visible keys [lo, hi), tile-relative
+      int lo = 0, hi = 0;
+      if (r < tile.y) {
+        const int sq = __ldg(a.rowseq + tile.x + r);
+        const int sst = __ldg(a.seq_start + sq) - tile.x, en = sst + __ldg(a.seq_len + sq);
+        lo = a.window >= 0 && r - a.window > sst ? r - a.window : sst;
+        hi = a.window >= 0 && r + a.window + 1 < en ? r + a.window + 1 : en;
+      }
+      if (!(ok = warp_wait(ok, &s_full[s], j & 1, a, abort_flag))) break;
+      tc_fence_after();
+      uint32_t mask[4];
+      bool any[4], all[4];
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        mask[ch] = chunk_mask(lo - 32 * ch, hi - 32 * ch);
+        any[ch] = __any_sync(0xffffffffu, mask[ch] != 0u);
+        all[ch] = __all_sync(0xffffffffu, mask[ch] == 0xffffffffu);
+      }
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int ch = 0; ch < 4; ++ch) {
+        if (!any[ch]) continue;
         uint32_t v[32];
         tmem_ld_32x32b_x32(t_row + 32 * ch, v);
         tmem_ld_wait();
-        float p[32];
         if (all[ch]) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) p[j] = fast_exp2(fmaf(u2f(v[j]), L2E, -ms));
+          for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], u2f(v[i]));
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            p[j] = fast_exp2((mask[ch] >> j) & 1u ? fmaf(u2f(v[j]), L2E, -ms) : -INFINITY);
-        }
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          sm[(j >> 1) & 3] += p[j] + p[j + 1];
-          w[j / 2] = pack_half2(p[j], p[j + 1]);
+          for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], (mask[ch] >> i) & 1u ? u2f(v[i]) : -INFINITY);
         }
       }
-      // chunk ch -> K atom ch / 2 (16 KB apart), 16-byte chunks 4 (ch % 2) ..
-      uint8_t* prow = sQ + (ch >> 1) * TILE_BYTES + r * 128;
+      const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float ms = (m == -INFINITY ? 0.0f : m) * L2E;
+      float sm[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int x = 0; x < 4; ++x)
-        *reinterpret_cast<uint4*>(prow + (((4 * (ch & 1) + x) ^ (r & 7)) << 4)) =
-            make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
+      for (int ch = 0; ch < 4; ++ch) {
+        uint32_t w[16];
+        if (!any[ch]) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) w[i] = 0u;
+        } else {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_row + 32 * ch, v);
+          tmem_ld_wait();
+          float p[32];
+          if (all[ch]) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) p[i] = fast_exp2(fmaf(u2f(v[i]), L2E, -ms));
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              p[i] = fast_exp2((mask[ch] >> i) & 1u ? fmaf(u2f(v[i]), L2E, -ms) : -INFINITY);
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            sm[(i >> 1) & 3] += p[i] + p[i + 1];
+            w[i / 2] = pack_half2(p[i], p[i + 1]);
+          }
+        }
+        // chunk ch -> K atom ch / 2 (the dead Q tile, then the dead K tile),
+        // 16-byte chunks 4 (ch % 2) .. of the row, swizzled
+        uint8_t* prow = st + (ch >> 1) * TILE_BYTES + r * 128;
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+          *reinterpret_cast<uint4*>(prow + (((4 * (ch & 1) + x) ^ (r & 7)) << 4)) =
+              make_uint4(w[4 * x], w[4 * x + 1], w[4 * x + 2], w[4 * x + 3]);
+      }
+      const float sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
+      fence_proxy_async_smem();  // P, before the tensor core reads it
+      tc_fence_before();         // S read before P.V overwrites it
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[s]);
+      if (!(ok = warp_wait(ok, &o_full[s], j & 1, a, abort_flag))) break;
+      tc_fence_after();
+      uint32_t o0[32], o1[32];
+      tmem_ld_32x32b_x32(t_row, o0);
+      tmem_ld_32x32b_x32(t_row + 32, o1);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_free[s]);
+      if (r < tile.y) {
+        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(tile.x + r) * 1024 + h * D);
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+          dst[x] = make_uint4(pack_half2(u2f(o0[8 * x]) * inv, u2f(o0[8 * x + 1]) * inv),
+                              pack_half2(u2f(o0[8 * x + 2]) * inv, u2f(o0[8 * x + 3]) * inv),
+                              pack_half2(u2f(o0[8 * x + 4]) * inv, u2f(o0[8 * x + 5]) * inv),
+                              pack_half2(u2f(o0[8 * x + 6]) * inv, u2f(o0[8 * x + 7]) * inv));
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+          dst[4 + x] = make_uint4(pack_half2(u2f(o1[8 * x]) * inv, u2f(o1[8 * x + 1]) * inv),
+                                  pack_half2(u2f(o1[8 * x + 2]) * inv, u2f(o1[8 * x + 3]) * inv),
+                                  pack_half2(u2f(o1[8 * x + 4]) * inv, u2f(o1[8 * x + 5]) * inv),
+                                  pack_half2(u2f(o1[8 * x + 6]) * inv, u2f(o1[8 * x + 7]) * inv));
+      }
     }
-    sum = (sm[0] + sm[1]) + (sm[2] + sm[3]);
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  if (__syncthreads_or(!ok)) ok = false;  // P complete, S read by all
-
-  // O = P . V over the dead S columns
-  if (ok && tid == 0) {
-    tc_fence_after();
-    const uint64_t dp = umma_desc_sw128(smem_u32(sQ));
-    const uint64_t dv = desc_mn_sw128(smem_u32(sV));
-#pragma unroll
-    for (int kk = 0; kk < TQ / 16; ++kk)
-      umma_f16(tmem, dp + static_cast<uint64_t>((kk >> 2) * (TILE_BYTES >> 4) + (kk & 3) * 2),
-               dv + static_cast<uint64_t>(kk * (2048 >> 4)), IDESC_PV, kk > 0);
-    umma_commit(o_bar);
-  }
-  if (ok) ok = mbar_wait_bounded(o_bar, 0, a.err, kErrAttnWait, nullptr, a.wait_limit_ns);
-  if (__syncthreads_or(!ok)) ok = false;
-  if (ok) {
-    tc_fence_after();
-    uint32_t o0[32], o1[32];
-    tmem_ld_32x32b_x32(t_row, o0);
-    tmem_ld_32x32b_x32(t_row + 32, o1);
-    tmem_ld_wait();
-    if (r < tile.y) {
-      const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
-      uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(tile.x + r) * 1024 + h * D);
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-        dst[x] = make_uint4(pack_half2(u2f(o0[8 * x]) * inv, u2f(o0[8 * x + 1]) * inv),
-                            pack_half2(u2f(o0[8 * x + 2]) * inv, u2f(o0[8 * x + 3]) * inv),
-                            pack_half2(u2f(o0[8 * x + 4]) * inv, u2f(o0[8 * x + 5]) * inv),
-                            pack_half2(u2f(o0[8 * x + 6]) * inv, u2f(o0[8 * x + 7]) * inv));
-#pragma unroll
-      for (int x = 0; x < 4; ++x)
-        dst[4 + x] = make_uint4(pack_half2(u2f(o1[8 * x]) * inv, u2f(o1[8 * x + 1]) * inv),
-                                pack_half2(u2f(o1[8 * x + 2]) * inv, u2f(o1[8 * x + 3]) * inv),
-                                pack_half2(u2f(o1[8 * x + 4]) * inv, u2f(o1[8 * x + 5]) * inv),
-                                pack_half2(u2f(o1[8 * x + 6]) * inv, u2f(o1[8 * x + 7]) * inv));
-    }
-  } else if (tid == 0) {
-    // a wait expired: MMAs and loads already issued land before teardown
-    umma_commit(drain);
-    mbar_wait_bounded(drain, 0, a.err, kErrAttnWait, nullptr, 0);
-    const unsigned long long t0 = global_ns();
-    while (global_ns() - t0 < 2000000ull) __nanosleep(1000);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (*abort_flag) {
+    // a wait expired somewhere: loads already in flight land before teardown
+    if (tid == 0) {
+      const unsigned long long t0 = global_ns();
+      while (global_ns() - t0 < 2000000ull) __nanosleep(1000);
+    }
+    __syncthreads();
+  }
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
@@ -269,9 +405,11 @@ __global__ void __launch_bounds__(THREADS, 4)
 
 }  // namespace
 
-cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArgs& a, cudaStream_t stream) {
+cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArgs& a, int num_sms,
+                                   cudaStream_t stream) {
   if (a.num_tiles <= 0) return cudaSuccess;
-  if (!a.tiles || !a.rowseq || !a.seq_start || !a.seq_len || !a.out || !a.err) return cudaErrorInvalidValue;
+  if (!a.tiles || !a.rowseq || !a.seq_start || !a.seq_len || !a.out || !a.err || num_sms <= 0)
+    return cudaErrorInvalidValue;
   static bool configured[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -282,7 +420,9 @@ cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArg
     if (e != cudaSuccess) return e;
     configured[dev] = true;
   }
-  return launch_pdl(attn_short_kernel, dim3(a.num_tiles, 16), dim3(THREADS), SMEM, stream, nullptr, 0, *tm_qkv, a);
+  const int units = a.num_tiles * 16;
+  const int grid = units < num_sms ? units : num_sms;
+  return launch_pdl(attn_short_kernel, dim3(grid), dim3(THREADS), SMEM, stream, nullptr, 0, *tm_qkv, a);
 }
 
 }  // namespace laya

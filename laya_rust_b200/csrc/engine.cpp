@@ -238,6 +238,18 @@ bool row_groups_enabled() {
 // (at most 4608: e.g. 9 row blocks x 2 parts, 3 x 6).
 constexpr int kPartRows = 4608;
 
+// The public forward replays a CUDA graph per request shape (captured on
+// the shape's second call); LAYA_FORWARD_GRAPHS=0 launches every forward
+// eagerly.  At most kForwardGraphs shapes are kept (least recently used out).
+constexpr size_t kForwardGraphs = 8;
+bool forward_graphs_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LAYA_FORWARD_GRAPHS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 bool splitk_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("LAYA_SPLITK");
@@ -477,8 +489,7 @@ struct GroupMaps {
 struct PlanMaps {
   GroupMaps g[2];
   CUtensorMap a_mk;                                // scorer A operand (gathered marker rows)
-  CUtensorMap qkv_tiles;                           // short-sequence attention: 64-column x 128-row boxes of qkv
-  CUtensorMap qkv_rows;                            // flash attention: 64-column x 32-row boxes of qkv
+  CUtensorMap qkv_rows;                            // attention: 64-column x 32-row boxes of qkv
   uint64_t gen = ~0ull;                            // arena generation encoded for
 };
 
@@ -580,8 +591,30 @@ struct Engine {
     ck(cudaEventRecord(ev, stream), "event record");
   }
 
+  // CUDA graphs of the public forward, keyed by everything a launch's
+  // arguments depend on (forward_graph_key); a shape is captured on its
+  // second call and replayed from then on.  Entries of an older arena
+  // generation (arena or RoPE tables moved, a weight uploaded) are dropped.
+  struct FwdGraph {
+    std::vector<int64_t> key;
+    cudaGraphExec_t exec = nullptr;
+    uint64_t gen = 0;
+    uint64_t last_use = 0;
+  };
+  std::vector<FwdGraph> fwd_graphs;
+  std::map<std::vector<int64_t>, int> fwd_seen;
+  uint64_t fwd_clock = 0;
+
+  void drop_forward_graphs() {
+    for (auto& g : fwd_graphs)
+      if (g.exec) cudaGraphExecDestroy(g.exec);
+    fwd_graphs.clear();
+    fwd_seen.clear();
+  }
+
   ~Engine() {
     if (stream) cudaStreamSynchronize(stream);
+    drop_forward_graphs();
     if (pinned_out) cudaFreeHost(pinned_out);
     if (staging) cudaFreeHost(staging);
     if (side) cudaStreamSynchronize(side);
@@ -727,6 +760,8 @@ struct Engine {
         ss[p * 32 + j] = sinf(b);
       }
     ck(cudaStreamSynchronize(stream), "sync");
+    // the tables move: graphs captured over the old ones must not replay
+    ++arena_gen;
     for (auto* pr : {&cos_full, &sin_full, &cos_slide, &sin_slide}) pr->alloc((size_t)n * 32 * 4, "rope alloc");
     ck(cudaMemcpy(cos_full.p, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
     ck(cudaMemcpy(sin_full.p, sf.data(), sf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
@@ -813,7 +848,6 @@ struct Engine {
     const uint64_t R = (uint64_t)p.R, nk = (uint64_t)p.n * p.k;
     const uint32_t ab = kGemmABoxRows, ob = kGemmOutBoxRows;
     bool bad = make_tmap_f16(&m.a_mk, mk16.p, nk, H, ab) != 0 ||
-               make_tmap_2d(&m.qkv_tiles, qkv.p, false, R, 3 * H, 64, kAttnTcQRows) != 0 ||
                make_tmap_2d(&m.qkv_rows, qkv.p, false, R, 3 * H, 64, kAttnTcBoxRows) != 0;
     for (size_t g = 0; g < p.groups.size() && !bad; ++g) {
       // each group's maps start at its first row and end at its last, so its
@@ -881,7 +915,7 @@ struct Engine {
         sa.stuck = 1;
         sa.wait_limit_ns = stuck_limit_ns;
       }
-      ck(launch_attention_short(&dp.maps.qkv_tiles, sa, s), "attention");
+      ck(launch_attention_short(&dp.maps.qkv_rows, sa, num_sms, s), "attention");
       ++nl;
       mark(kProfAttn);
     }
@@ -1263,6 +1297,72 @@ struct Engine {
     memcpy(act, pinned_out + nl, na * 4);
   }
 
+  // Everything the forward's launches take as arguments besides the plan
+  // buffer's contents: the batch shape, row groups and attention work
+  // counts (grids, tensor-map extents, split-K choices), the plan buffer's
+  // layout and address, and the arena generation.
+  std::vector<int64_t> forward_graph_key(const DevicePlan& dp) const {
+    const HostPlan& p = dp.host;
+    const PlanLayout& L = dp.lay;
+    std::vector<int64_t> k = {p.n, p.k, p.R, p.ntiles, p.nitems, (int64_t)arena_gen,
+                              (int64_t)(uintptr_t)dp.base, (int64_t)L.tok, (int64_t)L.pos, (int64_t)L.seq_start,
+                              (int64_t)L.seq_len, (int64_t)L.cls_row, (int64_t)L.mk_row, (int64_t)L.tiles,
+                              (int64_t)L.items, (int64_t)L.rowtype, (int64_t)L.mmask, (int64_t)L.rowseq,
+                              (int64_t)L.total, (int64_t)rope_len, parts_ready ? 1 : 0};
+    for (const RowGroup& g : p.groups) {
+      k.push_back(g.row0);
+      k.push_back(g.rows);
+      k.push_back(g.tile0);
+      k.push_back(g.ntiles);
+      k.push_back(g.item0);
+      k.push_back(g.nitems);
+    }
+    return k;
+  }
+
+  // The cached graph of this forward's shape, capturing it on the shape's
+  // second call; nullptr: run it eagerly.
+  cudaGraphExec_t forward_graph(DevicePlan& dp) {
+    if (!forward_graphs_enabled()) return nullptr;
+    fwd_graphs.erase(std::remove_if(fwd_graphs.begin(), fwd_graphs.end(),
+                                    [&](FwdGraph& g) {
+                                      if (g.gen == arena_gen) return false;
+                                      if (g.exec) cudaGraphExecDestroy(g.exec);
+                                      return true;
+                                    }),
+                     fwd_graphs.end());
+    const std::vector<int64_t> key = forward_graph_key(dp);
+    for (auto& g : fwd_graphs)
+      if (g.key == key) {
+        g.last_use = ++fwd_clock;
+        return g.exec;
+      }
+    if (fwd_seen.size() > 4096) fwd_seen.clear();
+    if (++fwd_seen[key] < 2) return nullptr;  // a shape seen once runs eagerly
+    cudaGraph_t graph = nullptr;
+    ck(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal), "begin capture");
+    try {
+      enqueue(dp);
+    } catch (...) {
+      cudaStreamEndCapture(stream, &graph);
+      if (graph) cudaGraphDestroy(graph);
+      throw;
+    }
+    ck(cudaStreamEndCapture(stream, &graph), "end capture");
+    cudaGraphExec_t exec = nullptr;
+    cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    ck(ie, "graph instantiate");
+    if (fwd_graphs.size() >= kForwardGraphs) {
+      auto lru = std::min_element(fwd_graphs.begin(), fwd_graphs.end(),
+                                  [](const FwdGraph& a, const FwdGraph& b) { return a.last_use < b.last_use; });
+      cudaGraphExecDestroy(lru->exec);
+      fwd_graphs.erase(lru);
+    }
+    fwd_graphs.push_back(FwdGraph{key, exec, arena_gen, ++fwd_clock});
+    return exec;
+  }
+
   void forward(const laya_req* q, float* logits, float* act, laya_tap_fn tap, void* user) {
     if (!finalized) throw Error(LAYA_E_STATE, "engine has no weights (call laya_finalize)");
     if (!logits || !act) throw Error(LAYA_E_INVALID, "null output buffer");
@@ -1271,7 +1371,13 @@ struct Engine {
     dp.host = make_plan(q);
     ensure_arena(dp.host);
     upload_plan(dp, true);
-    enqueue(dp, tap, user);
+    // taps read the stream between layers and the timeout test needs its
+    // stuck launch: both run eagerly
+    cudaGraphExec_t g = (tap || stuck_next) ? nullptr : forward_graph(dp);
+    if (g)
+      ck(cudaGraphLaunch(g, stream), "graph launch");
+    else
+      enqueue(dp, tap, user);
     read_outputs(dp.host, logits, act);
     if (tap) {
       tap(user, "logits", logits, (size_t)dp.host.n * dp.host.k);
@@ -1790,9 +1896,8 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
     laya::ck(cudaMemset(dout.p, 0, dout.bytes), "memset");
     derr.alloc(256, "err");
     laya::ck(cudaMemset(derr.p, 0, 256), "memset");
-    CUtensorMap tm128, tm32;
-    if (laya::make_tmap_2d(&tm128, dq.p, false, R, 3072, 64, laya::kAttnTcQRows) ||
-        laya::make_tmap_2d(&tm32, dq.p, false, R, 3072, 64, laya::kAttnTcBoxRows))
+    CUtensorMap tm32;
+    if (laya::make_tmap_2d(&tm32, dq.p, false, R, 3072, 64, laya::kAttnTcBoxRows))
       throw Error(LAYA_E_CUDA, "tensor map encode failed");
     laya::AttnShortArgs sa{};
     sa.out = dout.as<__half>();
@@ -1803,7 +1908,7 @@ int laya_selftest_attention(int device, const uint16_t* qkv, const int32_t* lens
     sa.num_tiles = (int)tiles.size();
     sa.window = window;
     sa.err = derr.as<int>();
-    laya::ck(laya::launch_attention_short(&tm128, sa, 0), "attention launch");
+    laya::ck(laya::launch_attention_short(&tm32, sa, num_sms, 0), "attention launch");
     laya::AttnArgs a{};
     a.out = dout.as<__half>();
     a.items = di.as<int4>();

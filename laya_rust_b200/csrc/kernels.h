@@ -112,9 +112,11 @@ struct AttnArgs {
   int stuck;              // timeout test: the producer first waits on a barrier nothing completes
 };
 // Sequences of at most kAttnTcQRows tokens: tiles (first row, rows) packing
-// whole consecutive sequences, one CTA per (tile, head), single pass; each
-// row sees only its own sequence (rowseq, seq_start, seq_len).  tm_qkv: box
-// 64 columns x kAttnTcQRows rows.
+// whole consecutive sequences; units (tile, head), single pass, four in
+// flight per SM on a persistent grid of min(16 * num_tiles, num_sms) CTAs;
+// each row sees only its own sequence (rowseq, seq_start, seq_len).  tm_qkv
+// is the same map as the flash kernel's (box 64 columns x kAttnTcBoxRows
+// rows).
 struct AttnShortArgs {
   __half* out;            // [R, 1024]
   const int2* tiles;      // [num_tiles]
@@ -127,7 +129,8 @@ struct AttnShortArgs {
   unsigned long long wait_limit_ns;
   int stuck;
 };
-cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArgs& a, cudaStream_t stream);
+cudaError_t launch_attention_short(const CUtensorMap* tm_qkv, const AttnShortArgs& a, int num_sms,
+                                   cudaStream_t stream);
 
 // Longer sequences: tcgen05 flash attention (persistent, min(16 * items, num_sms) CTAs); tm_qkv
 // maps the qkv buffer ([R, 3072] f16, box 64 columns x kAttnTcBoxRows rows,

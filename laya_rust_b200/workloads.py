@@ -157,6 +157,18 @@ def assign_requests(requests, world: int):
     return out
 
 
+def assign_by_cost(costs, world: int):
+    """The same greedy rule over plain per-request token costs (in dispatch
+    order, ties to the lowest rank): the request indices per GPU."""
+    load = [0] * world
+    out = [[] for _ in range(world)]
+    for ri, c in enumerate(costs):
+        g = min(range(world), key=lambda i: (load[i], i))
+        out[g].append(ri)
+        load[g] += c
+    return out
+
+
 def pack_stream(requests, max_tokens: int = 16384):
     """Cross-request packing in dispatch order: items join the current forward
     while max_len * count stays within the budget (the budget rule of

@@ -1,0 +1,65 @@
+"""The public forward's CUDA-graph cache (laya_forward): a request shape is
+launched eagerly the first time, captured on its second call and replayed
+after that.  A replay reads the request through the same device buffer, so
+it must give bitwise the eager forward's logits and act -- for the request it
+was captured on and for any other request of the same shape -- and a weight
+uploaded again must retire the graph (it holds the old weight pointers)."""
+import numpy as np
+import pytest
+
+from laya_rust_b200 import engine as E
+from laya_rust_b200 import modelgen
+from test_gpu_parity import synthetic_req
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def engine():
+    e = E.Engine(modelgen.cached_model(seed=0), device=0)
+    yield e
+    e.close()
+
+
+def eager(engine, req):
+    # a tapped forward always runs eagerly
+    return engine.forward(req, taps={})
+
+
+def same(a, b):
+    return np.array_equal(a.logits, b.logits) and np.array_equal(a.act, b.act)
+
+
+def test_replays_match_the_eager_forward_bitwise(engine):
+    shapes = [[200, 150, 70, 100], [31, 77, 128, 64, 90, 12]]
+    reqs = [synthetic_req(70 + i, lens, 4) for i, lens in enumerate(shapes)]
+    want = [eager(engine, r) for r in reqs]
+    for _ in range(3):   # first sight (eager), second (capture), then replays
+        for r, w in zip(reqs, want):
+            assert same(engine.forward(r), w)
+    # another request of a captured shape: new ids, markers and question types
+    other = synthetic_req(99, shapes[0], 4)
+    assert not np.array_equal(other.ids, reqs[0].ids)
+    assert same(engine.forward(other), eager(engine, other))
+
+
+def test_a_weight_uploaded_again_retires_the_graph():
+    eng = E.Engine(modelgen.cached_model(seed=0), device=0)
+    try:
+        req = synthetic_req(5, [120, 60, 33], 3)
+        for _ in range(3):
+            eng.forward(req)                 # captured and replayed
+        eng.upload_f32("scorer.3.bias", np.array([0.5], np.float32))
+        got = eng.forward(req)
+        want = eager(eng, req)
+        assert same(got, want)
+        mm = req.mmask != 0
+        before = E.Engine(modelgen.cached_model(seed=0), device=0)
+        try:
+            base = before.forward(req)
+        finally:
+            before.close()
+        # scorer.3.bias is 0 in the model: every valid logit moved by 0.5
+        assert np.allclose(got.logits[mm.ravel()], base.logits[mm.ravel()] + 0.5, atol=1e-5)
+    finally:
+        eng.close()

@@ -60,3 +60,15 @@ def test_long_state_has_a_32_token_head():
     for b in range(req.n):
         assert ids[b, 32] == arch.SEP_ID
         assert np.all(req.mpos.reshape(req.n, req.k)[b] > 32)
+
+
+def test_assignment_by_cost_partitions_and_balances():
+    rng = np.random.default_rng(3)
+    costs = [int(c) for c in rng.integers(20, 1100, 1024)]
+    for world in (1, 2, 4, 8):
+        parts = workloads.assign_by_cost(costs, world)
+        assert sorted(i for p in parts for i in p) == list(range(len(costs)))
+        loads = [sum(costs[i] for i in p) for p in parts]
+        assert max(loads) - min(loads) <= max(costs)
+        for p in parts:
+            assert p == sorted(p)   # each GPU keeps dispatch order
