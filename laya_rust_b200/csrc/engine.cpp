@@ -198,7 +198,7 @@ struct DevBuf {
 struct Weight {
   DevBuf buf;
   CUtensorMap tmap;         // Linear weights only
-  CUtensorMap tmap_narrow;  // Linear weights with 1024 rows: box for 256 x 128 tiles
+  CUtensorMap tmap_narrow;  // Linear weights: box for 256 x 128 tiles (small batches)
   std::vector<float> host;  // small tensors the host also needs (rope, scorer bias)
   bool present = false;
 };
@@ -245,6 +245,16 @@ constexpr size_t kForwardGraphs = 8;
 bool forward_graphs_enabled() {
   static const bool on = [] {
     const char* v = std::getenv("LAYA_FORWARD_GRAPHS");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// Narrow (256 x 128) tiles for the f16-output GEMMs of small batches;
+// LAYA_NARROW=0 keeps 256 x 256 tiles everywhere.
+bool narrow_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LAYA_NARROW");
     return !(v && v[0] == '0');
   }();
   return on;
@@ -686,7 +696,7 @@ struct Engine {
           const uint64_t kdim = (uint64_t)role.shape[1];
           if (make_tmap_f16(&wt.tmap, wt.buf.p, rows, kdim, kGemmBBoxRows) != 0)
             throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
-          if (rows == (uint64_t)H && make_tmap_f16(&wt.tmap_narrow, wt.buf.p, rows, kdim, kGemmBBoxRowsNarrow) != 0)
+          if (make_tmap_f16(&wt.tmap_narrow, wt.buf.p, rows, kdim, kGemmBBoxRowsNarrow) != 0)
             throw Error(LAYA_E_CUDA, "tensor map encode failed for " + name);
         }
         break;
@@ -881,10 +891,14 @@ struct Engine {
       a.wait_limit_ns = stuck_limit_ns;
       stuck_next = false;
     }
-    // 256 x 128 tiles (twice the tiles per wave for N = 1024) measured slower
-    // than 256 x 256 on the residual GEMMs: the smaller stages leave the TMA
-    // latency exposed.  They stay available through launch_gemm's `bn`.
-    const bool narrow = false;
+    // 256 x 128 tiles for the f16-output GEMMs of small batches, whose
+    // 256 x 256 tiles would fill at most half the clusters: twice the
+    // clusters stream the weights.  Large batches keep 256 x 256 (256 x 128
+    // measured slower there: the smaller stages leave the TMA latency
+    // exposed); the residual GEMMs of small batches split K instead.
+    const int tiles256 = ((M + kGemmBM - 1) / kGemmBM) * (N / kGemmBN);
+    const bool narrow = narrow_enabled() && tiles256 * 2 <= num_sms / 2 &&
+                        (epi == kEpiQkvRope || epi == kEpiQkvBias || epi == kEpiGeglu || epi == kEpiBiasRelu);
     ck(launch_gemm(epi, GemmMaps{&A, narrow ? &Wt.tmap_narrow : &Wt.tmap, &Out, out2}, a, num_sms, s,
                    narrow ? kGemmBNNarrow : kGemmBN),
        "gemm launch");

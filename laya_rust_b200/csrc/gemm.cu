@@ -362,6 +362,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       st.store(tmOut, n0 + c0, row0 + yoff, reduce);
     }
   } else if constexpr (EPI == kEpiGeglu) {
+    // narrow tiles (64 gate | 64 up columns): the column-half-0 warps write
+    // all 64 outputs, the other four have none
+    if (BN == kGemmBNNarrow && hc == 1) return;
     const int oc0 = (n0 / BN) * (BN / 2);
 #pragma unroll 1
     for (int c0 = cb / 2; c0 < ce / 2; c0 += 64) {
@@ -482,7 +485,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int u = cluster_id; u < num_units && ok; u += num_clusters) {
         const Unit w = unit_of<EPI>(u, args, num_kb);
         const int m0 = (w.tile / num_n) * BM + static_cast<int>(rank) * CTA_ROWS;
-        const int n0 = (w.tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
+        int n0 = (w.tile % num_n) * BN + static_cast<int>(rank) * (BN / 2);
+        if constexpr (EPI == kEpiGeglu && BN == kGemmBNNarrow) {
+          // a narrow GeGLU tile t pairs 64 gate rows with their 64 up rows:
+          // in the co-tiled weight (256-row groups: 128 gate | 128 up) those
+          // are rows 256 (t / 2) + 64 (t % 2) (CTA 0) and 128 further (CTA 1)
+          const int t = w.tile % num_n;
+          n0 = 256 * (t >> 1) + 128 * static_cast<int>(rank) + 64 * (t & 1);
+        }
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, args.err, kErrGemmProducerWait, abort_flag,
                                  args.wait_limit_ns)) {
@@ -652,10 +662,17 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
       return cudaErrorInvalidValue;
   }
   if (bn == kGemmBNNarrow) {
-    // narrow tiles: the residual GEMMs with N = 1024 (more tiles per wave)
-    if (epilogue == kEpiResid) return launch_one<kEpiResid, kGemmBNNarrow>(m, args, num_sms, stream);
-    if (epilogue == kEpiStoreF32) return launch_one<kEpiStoreF32, kGemmBNNarrow>(m, args, num_sms, stream);
-    return cudaErrorInvalidValue;
+    // narrow 256 x 128 tiles: twice the tiles per wave, for small M where a
+    // GEMM's 256-column tiles leave most clusters idle
+    switch (epilogue) {
+      case kEpiQkvRope: return launch_one<kEpiQkvRope, kGemmBNNarrow>(m, args, num_sms, stream);
+      case kEpiQkvBias: return launch_one<kEpiQkvBias, kGemmBNNarrow>(m, args, num_sms, stream);
+      case kEpiResid: return launch_one<kEpiResid, kGemmBNNarrow>(m, args, num_sms, stream);
+      case kEpiGeglu: return launch_one<kEpiGeglu, kGemmBNNarrow>(m, args, num_sms, stream);
+      case kEpiBiasRelu: return launch_one<kEpiBiasRelu, kGemmBNNarrow>(m, args, num_sms, stream);
+      case kEpiStoreF32: return launch_one<kEpiStoreF32, kGemmBNNarrow>(m, args, num_sms, stream);
+      default: return cudaErrorInvalidValue;
+    }
   }
   switch (epilogue) {
     case kEpiQkvRope: return launch_one<kEpiQkvRope, kGemmBN>(m, args, num_sms, stream);
