@@ -217,6 +217,16 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "r"(taddr));
 }
 
+// 32 lanes x 16 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32"
+      " {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -245,6 +255,13 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);    // M / 16
 }
 
+// 2^x by the hardware's approximate exponential (one MUFU op).
+__device__ __forceinline__ float exp2f_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // erf by Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7), the approximation
 // the reference CPU backend uses (backend/cpu/mod.rs:59-74, there in f64):
 //   erf(x) = 1 - t (a1 + t (a2 + t (a3 + t (a4 + t a5)))) exp(-x^2),
@@ -260,6 +277,58 @@ __device__ __forceinline__ float erf_as(float x) {
 __device__ __forceinline__ float gelu_erf(float v) {
   // exact-erf GELU (cpu/mod.rs:76-78): 0.5 v (1 + erf(v / sqrt 2))
   return 0.5f * v * (1.0f + erf_as(v * 0.70710678118654752f));
+}
+
+// ---- packed f32 pairs (sm_100 f32x2 arithmetic: two lanes per instruction, each
+// rounded as the scalar f32 operation) --------------------------------------------
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_get(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_splat(float v) { return f2(v, v); }
+
+// (gelu_erf(v0), gelu_erf(v1)) in packed pairs: the same A&S 7.1.26 formula,
+// with the polynomial's coefficients negated so that erf(|x|) = 1 + p e is
+// one fused step.  The divide and the exponential stay per lane (MUFU).
+__device__ __forceinline__ uint64_t gelu_erf2(uint64_t v) {
+  const uint64_t x = f2_mul(v, f2_splat(0.70710678118654752f));
+  float x0, x1;
+  f2_get(x, x0, x1);
+  const uint64_t ax = f2(fabsf(x0), fabsf(x1));
+  float d0, d1;
+  f2_get(f2_fma(ax, f2_splat(0.3275911f), f2_splat(1.0f)), d0, d1);
+  const uint64_t t = f2(__fdividef(1.0f, d0), __fdividef(1.0f, d1));
+  uint64_t p = f2_fma(t, f2_splat(-1.061405429f), f2_splat(1.453152027f));
+  p = f2_fma(t, p, f2_splat(-1.421413741f));
+  p = f2_fma(t, p, f2_splat(0.284496736f));
+  p = f2_fma(t, p, f2_splat(-0.254829592f));
+  p = f2_mul(t, p);  // -t (a1 + t (a2 + t (a3 + t (a4 + t a5))))
+  float e0, e1;
+  f2_get(f2_mul(f2_mul(ax, ax), f2_splat(-1.4426950408889634f)), e0, e1);
+  float r0, r1;
+  f2_get(f2_fma(p, f2(exp2f_approx(e0), exp2f_approx(e1)), f2_splat(1.0f)), r0, r1);
+  const uint64_t erf = f2(copysignf(r0, x0), copysignf(r1, x1));
+  const uint64_t h = f2_mul(v, f2_splat(0.5f));
+  return f2_fma(h, erf, h);
 }
 
 // ---- programmatic dependent launch ---------------------------------------------------

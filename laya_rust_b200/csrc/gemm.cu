@@ -195,17 +195,6 @@ __device__ __forceinline__ void stage_row(uint8_t* stage, int r, const uint32_t 
     *reinterpret_cast<uint4*>(row + ((j ^ (r & 7)) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
 }
 
-// Half a row (64 B, chunks [8h, 8h+4) of 16 B): used when 32 f16 values
-// fill one half of a 128-byte staging row.
-__device__ __forceinline__ void stage_half_row(uint8_t* stage, int r, int h, const uint32_t (&w)[16]) {
-  uint8_t* row = stage + r * 128;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int c = 4 * h + j;
-    *reinterpret_cast<uint4*>(row + ((c ^ (r & 7)) << 4)) = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
-  }
-}
-
 // Per-warp epilogue state: one staging buffer, refilled once the previous
 // TMA store from it has read it.  `active` is false for a 32-row slab that
 // lies wholly past the last row (nothing is stored).
@@ -272,16 +261,20 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
   if constexpr (EPI == kEpiQkvRope) {
     const int part = n0 / 1024;
     if (part < 2) {
-      float cs[32], sn[32];
       const int p = valid ? a.pos[row] : 0;
       const float4* c4 = reinterpret_cast<const float4*>(a.cosb + p * 32);
       const float4* s4 = reinterpret_cast<const float4*>(a.sinb + p * 32);
+      // (cos, sin) of the row's position for dims j, j + 1, as packed pairs
+      uint64_t cs2[16], sn2[16];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        float4 c = __ldg(c4 + i), s = __ldg(s4 + i);
-        cs[4 * i] = c.x; cs[4 * i + 1] = c.y; cs[4 * i + 2] = c.z; cs[4 * i + 3] = c.w;
-        sn[4 * i] = s.x; sn[4 * i + 1] = s.y; sn[4 * i + 2] = s.z; sn[4 * i + 3] = s.w;
+        const float4 c = __ldg(c4 + i), s = __ldg(s4 + i);
+        cs2[2 * i] = f2(c.x, c.y);
+        cs2[2 * i + 1] = f2(c.z, c.w);
+        sn2[2 * i] = f2(s.x, s.y);
+        sn2[2 * i + 1] = f2(s.z, s.w);
       }
+      const uint64_t sc2 = f2_splat(a.scale);
 #pragma unroll 1
       for (int hh = cb / 64; hh < ce / 64; ++hh) {
         uint32_t lo[32], hi[32];
@@ -291,10 +284,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
         uint32_t w[32];
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
-          // rotate-half RoPE: d < 32: q*c - q[d+32]*s ; d >= 32: q*c + q[d-32]*s
-          const float a0 = u2f(lo[j]), b0 = u2f(hi[j]), a1 = u2f(lo[j + 1]), b1 = u2f(hi[j + 1]);
-          w[j / 2] = pack_half2((a0 * cs[j] - b0 * sn[j]) * a.scale, (a1 * cs[j + 1] - b1 * sn[j + 1]) * a.scale);
-          w[16 + j / 2] = pack_half2((b0 * cs[j] + a0 * sn[j]) * a.scale, (b1 * cs[j + 1] + a1 * sn[j + 1]) * a.scale);
+          // rotate-half RoPE, two dims per packed step:
+          //   d < 32: (q c - q[d+32] s) scale ; d >= 32: (q c + q[d-32] s) scale
+          const uint64_t A = f2(u2f(lo[j]), u2f(lo[j + 1])), B = f2(u2f(hi[j]), u2f(hi[j + 1]));
+          const uint64_t C = cs2[j / 2], S = sn2[j / 2];
+          float r0, r1, s0, s1;
+          f2_get(f2_mul(f2_sub(f2_mul(A, C), f2_mul(B, S)), sc2), r0, r1);
+          f2_get(f2_mul(f2_fma(A, S, f2_mul(B, C)), sc2), s0, s1);
+          w[j / 2] = pack_half2(r0, r1);
+          w[16 + j / 2] = pack_half2(s0, s1);
         }
         uint8_t* s = st.acquire();
         stage_row(s, r, w);
@@ -369,20 +367,25 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
 #pragma unroll 1
     for (int c0 = cb / 2; c0 < ce / 2; c0 += 64) {
       if (oc0 + c0 >= a.n_valid) break;
-      uint32_t w[2][16];
+      // 16 gate and 16 up columns per TMEM load: the 64 outputs' GELU
+      // chains then fit in registers and interleave
+      uint32_t w[32];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t g[32], u[32];
-        tmem_ld_32x32b_x32(t_row + c0 + 32 * h, g);
-        tmem_ld_32x32b_x32(t_row + BN / 2 + c0 + 32 * h, u);
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t g[16], u[16];
+        tmem_ld_32x32b_x16(t_row + c0 + 16 * q4, g);
+        tmem_ld_32x32b_x16(t_row + BN / 2 + c0 + 16 * q4, u);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; j += 2)
-          w[h][j / 2] = pack_half2(gelu_erf(u2f(g[j])) * u2f(u[j]), gelu_erf(u2f(g[j + 1])) * u2f(u[j + 1]));
+        for (int j = 0; j < 16; j += 2) {
+          // two columns per packed step: gelu(gate) . up
+          float y0, y1;
+          f2_get(f2_mul(gelu_erf2(f2(u2f(g[j]), u2f(g[j + 1]))), f2(u2f(u[j]), u2f(u[j + 1]))), y0, y1);
+          w[8 * q4 + j / 2] = pack_half2(y0, y1);
+        }
       }
       uint8_t* s = st.acquire();
-      stage_half_row(s, r, 0, w[0]);
-      stage_half_row(s, r, 1, w[1]);
+      stage_row(s, r, w);
       st.store(tmOut, oc0 + c0, row0, false);
     }
   } else {  // kEpiScorer
