@@ -63,3 +63,18 @@ def test_a_weight_uploaded_again_retires_the_graph():
         assert np.allclose(got.logits[mm.ravel()], base.logits[mm.ravel()] + 0.5, atol=1e-5)
     finally:
         eng.close()
+
+
+def test_a_longer_request_retires_the_graphs():
+    """A request longer than any before grows the RoPE tables (reallocated);
+    graphs captured over the old tables must not replay."""
+    eng = E.Engine(modelgen.cached_model(seed=0), device=0)
+    try:
+        short = synthetic_req(11, [100, 80, 64], 3)
+        for _ in range(3):
+            eng.forward(short)               # captured and replayed
+        eng.forward(synthetic_req(12, [600], 3))  # RoPE tables 512 -> 1024 rows
+        for _ in range(3):                   # eager, captured again, replayed
+            assert same(eng.forward(short), eager(eng, short))
+    finally:
+        eng.close()
