@@ -147,8 +147,14 @@ __device__ __forceinline__ void chunk_p(uint8_t* st, int r, int ch, const uint32
 #pragma unroll
     for (int i = 0; i < 16; ++i) w[i] = 0u;
   } else if (all) {
+    // s log2 e - max for two keys per packed step
+    const uint64_t l2e2 = f2_splat(L2E), nms2 = f2_splat(-ms);
 #pragma unroll
-    for (int i = 0; i < 32; i += 2) w[i / 2] = exp2_h2(fmaf(u2f(v[i]), L2E, -ms), fmaf(u2f(v[i + 1]), L2E, -ms));
+    for (int i = 0; i < 32; i += 2) {
+      float a0, a1;
+      f2_get(f2_fma(f2(u2f(v[i]), u2f(v[i + 1])), l2e2, nms2), a0, a1);
+      w[i / 2] = exp2_h2(a0, a1);
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 32; i += 2)

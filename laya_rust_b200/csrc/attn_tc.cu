@@ -569,9 +569,14 @@ __global__ void __launch_bounds__(THREADS, 1)
               tmem_ld_32x32b_x32(t_s + 32 * ch, v);
               tmem_ld_wait();
               if (ch ? all1 : all0) {
+                // s log2 e - max for two keys per packed step
+                const uint64_t l2e2 = f2_splat(L2E), nms2 = f2_splat(-ms);
 #pragma unroll
-                for (int j = 0; j < 32; j += 2)
-                  w[j / 2] = exp2_h2(fmaf(u2f(v[j]), L2E, -ms), fmaf(u2f(v[j + 1]), L2E, -ms));
+                for (int j = 0; j < 32; j += 2) {
+                  float a0, a1;
+                  f2_get(f2_fma(f2(u2f(v[j]), u2f(v[j + 1])), l2e2, nms2), a0, a1);
+                  w[j / 2] = exp2_h2(a0, a1);
+                }
               } else {
 #pragma unroll
                 for (int j = 0; j < 32; j += 2)

@@ -397,8 +397,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       tmem_ld_wait();
       const float* b = a.bias + n0 + c0;
       const float* w = a.wvec + n0 + c0;
+      // two columns per packed step; the two running sums are added at the end
+      uint64_t acc2 = f2_splat(0.0f);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) s += gelu_erf(u2f(v[j]) + __ldg(b + j)) * __ldg(w + j);
+      for (int j = 0; j < 32; j += 2) {
+        const uint64_t g = gelu_erf2(f2(u2f(v[j]) + __ldg(b + j), u2f(v[j + 1]) + __ldg(b + j + 1)));
+        acc2 = f2_fma(g, f2(__ldg(w + j), __ldg(w + j + 1)), acc2);
+      }
+      float s0, s1;
+      f2_get(acc2, s0, s1);
+      s += s0 + s1;
     }
     if (valid) static_cast<float*>(a.out)[static_cast<size_t>(2 * (n0 / BN) + hc) * a.ldo + row] = s;
   }
