@@ -42,8 +42,10 @@
 //               P = 2^(s log2 e - max) with the packed f16 exponential into
 //               its half of the row of P (the swizzled K-major operand
 //               layout, one 64-key atom per half) and rescales its columns of
-//               the row's O (and the sum column) in TMEM when the maximum
-//               grew.  After the unit's last block each half scales its 32
+//               the row's O (and the sum column) in TMEM when the maximum P
+//               is taken against moved -- only when a block's maximum exceeds
+//               it by more than 8 in log2 units, so P <= 256 and most blocks
+//               skip the rescale.  After the unit's last block each half scales its 32
 //               of the row's 64 outputs by 1 / sum and stores them.
 // Shared memory: Q 2 x 16 KB, K 3 x 16 KB, V 3 x 16 KB, ones 16 KB, P 2 x 32
 // KB, the CTA's first 64 work items, the max exchange (about 212 KB).
@@ -94,6 +96,9 @@ constexpr int TMEM_COLS = 512;
 constexpr int S_COL = 0;                 // S[slot] at slot * 128
 constexpr int O_COL = 256;               // O[slot] at 256 + slot * 128 (80 used)
 constexpr float L2E = 1.4426950408889634f;
+// 8 in log2 units: the most a row's scores may exceed the maximum its P is
+// taken against before O is rescaled (P <= 256)
+constexpr float kRescaleSlack = 8.0f / L2E;
 
 // S: A = Q (K-major), B = K block (K-major), M = 128, N = 128
 constexpr uint32_t IDESC_QK = umma_idesc_f16(TQ, TK);
@@ -542,12 +547,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         named_sync(bar_id, 64);
         const float mo = xmax_s[(par * 2 + (half ^ 1)) * TQ + row];
         par ^= 1;
-        const float m_new = fmaxf(m_run, fmaxf(mh, mo));
+        // The maximum P is taken against moves only when the block's
+        // maximum exceeds it by more than kRescaleSlack: P = 2^((s - m) log2 e)
+        // then stays at most 2^8 (f16 holds it to the same relative
+        // precision), and O and its row sum, accumulated against the same m,
+        // give the same quotient -- so most blocks need no rescale of O.
+        const float m_blk = fmaxf(mh, mo);
+        const float m_new = (m_run == -INFINITY || m_blk > m_run + kRescaleSlack) ? fmaxf(m_run, m_blk) : m_run;
         const float m_use = m_new == -INFINITY ? 0.0f : m_new;
         const float ms = m_use * L2E;
         // O (sums included) was accumulated against m_run: rescale by
-        // 2^((m_run - m_new) log2 e)
-        const float alpha = m_run == -INFINITY ? 0.0f : fast_exp2((m_run - m_use) * L2E);
+        // 2^((m_run - m_new) log2 e) when m moved; while m_run is -inf every
+        // earlier P of the row was 0, so O is 0 and needs none
+        const float alpha =
+            (m_new == m_run || m_run == -INFINITY) ? 1.0f : fast_exp2((m_run - m_use) * L2E);
         // the slot's previous P.V must be done: P is rewritten and O rescaled
         if (jj > 0) {
           ok = warp_wait(ok, &pv_done[slot], pv_phase, a, abort_flag);
