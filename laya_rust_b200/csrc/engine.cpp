@@ -969,13 +969,16 @@ struct Engine {
   // (a LayerNorm of the same rows comes next) and a small M, the K loop is
   // split and the sums stay pending for that LayerNorm.
   void resid_gemm(int gi, const CUtensorMap& A, const Weight& Wt, const CUtensorMap& Out, int R, int K, cudaStream_t s,
-                  int64_t& nl, int kind, bool defer) {
+                  int64_t& nl, int kind, bool defer, const float* bias = nullptr) {
     GemmArgs r{};
     r.ldo = H;
+    r.bias = bias;
     const int S = defer ? choose_splits(R, K) : 1;
     if (S < 2) {
       int tail_rb = 0, ts = 0;
-      if (defer) choose_tail(R, K, tail_rb, ts);
+      // the tail split adds whole tiles and parts into different places:
+      // a bias would be added by every part, so biased GEMMs add whole tiles
+      if (defer && !bias) choose_tail(R, K, tail_rb, ts);
       if (ts < 2) {
         gemm(kEpiResid, A, Wt, Out, R, H, K, r, s, nl, kind);
         return;
@@ -1083,19 +1086,18 @@ struct Engine {
     q.scale = SCALE;
     gemm(kEpiQkvBias, M.a_t16, W(hn(hl, "self_attn.in_proj_weight")), M.o_qkv, R, 3 * H, H, q, s, nl, kProfHead);
     attention(dp, gi, -1, s, nl);
-    GemmArgs r{};
-    r.ldo = H;
-    r.bias = W(hn(hl, "self_attn.out_proj.bias")).buf.as<float>();
-    gemm(kEpiResid, M.a_ctx, W(hn(hl, "self_attn.out_proj.weight")), M.o_x, R, H, H, r, s, nl, kProfHead);
+    resid_gemm(gi, M.a_ctx, W(hn(hl, "self_attn.out_proj.weight")), M.o_x, R, H, s, nl, kProfHead, true,
+               W(hn(hl, "self_attn.out_proj.bias")).buf.as<float>());
     row_ln(gi, xg, hn(hl, "norm2.weight"), W(hn(hl, "norm2.bias")).buf.as<float>(), tg, R, s, nl);
     GemmArgs f{};
     f.ldo = HEAD_INTER;
     f.bias = W(hn(hl, "linear1.bias")).buf.as<float>();
     gemm(kEpiBiasRelu, M.a_t16, W(hn(hl, "linear1.weight")), M.o_hmlp, R, HEAD_INTER, H, f, s, nl, kProfHead);
-    GemmArgs r2{};
-    r2.ldo = H;
-    r2.bias = W(hn(hl, "linear2.bias")).buf.as<float>();
-    gemm(kEpiResid, M.a_hmlp, W(hn(hl, "linear2.weight")), M.o_x, R, H, HEAD_INTER, r2, s, nl, kProfHead);
+    // its split-K parts (small batches) stay pending for the next head
+    // layer's norm1; after the last head layer they are folded in before the
+    // scorer's gathered LayerNorm
+    resid_gemm(gi, M.a_hmlp, W(hn(hl, "linear2.weight")), M.o_x, R, HEAD_INTER, s, nl, kProfHead, true,
+               W(hn(hl, "linear2.bias")).buf.as<float>());
   }
 
   // Scorer over the gathered marker rows and the act head (graph.rs:154-186),
@@ -1184,8 +1186,12 @@ struct Engine {
     if (tap) emit_rows(dp, "final", tap, user);
     for (int hl = 0; hl < HEAD_LAYERS; ++hl) {
       for (int gi = 0; gi < G; ++gi) head_layer(dp, gi, hl, group_stream(gi, conc), nl);
-      if (tap) emit_rows(dp, fmt("head.%d", hl).c_str(), tap, user);
+      if (tap) {
+        for (int gi = 0; gi < G; ++gi) fold_parts(dp, gi, group_stream(gi, conc), nl);
+        emit_rows(dp, fmt("head.%d", hl).c_str(), tap, user);
+      }
     }
+    for (int gi = 0; gi < G; ++gi) fold_parts(dp, gi, group_stream(gi, conc), nl);
     join(conc);
     scorer_tail(dp, stream, nl);
     if (pend[0].nparts || pend[1].nparts) throw Error(LAYA_E_STATE, "split-K parts left pending after the forward");

@@ -348,7 +348,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c0, v);
       tmem_ld_wait();
-      if (EPI == kEpiResid && a.bias) {
+      // a bias is added once: by the whole tile, or by K part 0 (yoff 0)
+      if ((EPI == kEpiResid || (EPI == kEpiPartial && yoff == 0)) && a.bias) {
         const float* b = a.bias + n0 + c0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(u2f(v[j]) + __ldg(b + j));

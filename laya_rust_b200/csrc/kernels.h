@@ -34,9 +34,9 @@ enum GemmEpilogue : int {
   kEpiScorer = 5,   // f32 partial[N/256][ldo] = sum_c gelu(acc + bias) * wvec
   kEpiStoreF32 = 6, // f32 out [M, N] = acc (tests)
   // split-K partial sums: the K range is cut into `splits` parts and part s of
-  // tile (m, n) stores its f32 sum at output rows s * split_rows + m.  A row
-  // kernel adds the parts to the residual in part order (deterministic), so
-  // small-M GEMMs spread their K loop over more SMs.
+  // tile (m, n) stores its f32 sum at output rows s * split_rows + m (part 0
+  // adds `bias`, if any).  A row kernel adds the parts to the residual in part
+  // order (deterministic), so small-M GEMMs spread their K loop over more SMs.
   kEpiPartial = 7,
   // residual GEMM whose tiles do not fill the last wave: work units below
   // main_tiles are whole tiles reduce-added into x (kEpiResid, no bias);

@@ -265,6 +265,93 @@ __global__ void __launch_bounds__(256) final_ln_kernel(float* x, const float* wf
   store_f16(t16 + static_cast<size_t>(row) * HID, lane, v);
 }
 
+// ---- small batches: one 128-thread CTA per row ---------------------------------------
+// With few rows the one-warp-per-row kernels run on few SMs and each warp
+// walks a long dependent chain (the row, then its split-K parts).  Here a
+// row's 1024 values are spread over 128 threads (two float4 each, 512-byte
+// coalesced), so a 179-row batch keeps 179 SMs loading at once.  The
+// arithmetic is the same as the warp kernels' (parts summed in part order,
+// then added; two-pass f32 statistics), with the sums reduced over the block
+// in a fixed order.
+constexpr int kSmallRows = 1024;  // batches below this many rows take the per-row CTAs
+constexpr int kRowThreads = 128;
+
+// Sum over the CTA's 128 threads, the same value in every thread.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red is free (an earlier reduction has been read)
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  return (red[0] + red[1]) + (red[2] + red[3]);
+}
+
+template <int NP>
+__global__ void __launch_bounds__(kRowThreads) ln_row_cta_kernel(float* x, const int* idx, const PendingParts p,
+                                                                 const float* w, const float* b, float eps,
+                                                                 __half* t16, int rows) {
+  __shared__ float red[4];
+  grid_dep_wait();
+  grid_dep_trigger();
+  const int row = blockIdx.x, t = threadIdx.x;
+  if (row >= rows) return;
+  const int src = idx ? idx[row] : row;
+  float4* xr = reinterpret_cast<float4*>(x + static_cast<size_t>(src) * HID);
+  const uint64_t pol = l2_evict_last();
+  float4 v[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v[i].x), "=f"(v[i].y), "=f"(v[i].z), "=f"(v[i].w)
+                 : "l"(xr + t + 128 * i), "l"(pol));
+  if constexpr (NP > 0) {
+    if (row >= p.row0) {
+      // parts summed in part order, then added (as add_parts)
+      const float4* q = reinterpret_cast<const float4*>(p.parts + static_cast<size_t>(row - p.row0) * HID);
+      const size_t st4 = p.stride / 4;
+      float4 f[NP][2];
+#pragma unroll
+      for (int s = 0; s < NP; ++s)
+#pragma unroll
+        for (int i = 0; i < 2; ++i) f[s][i] = ld_stream_f4(q + s * st4 + t + 128 * i);
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        float4 a = f[0][i];
+#pragma unroll
+        for (int s = 1; s < NP; ++s) {
+          a.x += f[s][i].x; a.y += f[s][i].y; a.z += f[s][i].z; a.w += f[s][i].w;
+        }
+        v[i].x += a.x; v[i].y += a.y; v[i].z += a.z; v[i].w += a.w;
+        xr[t + 128 * i] = v[i];
+      }
+    }
+  }
+  const float mean = block_sum((v[0].x + v[0].y) + (v[0].z + v[0].w) + (v[1].x + v[1].y) + (v[1].z + v[1].w), red) *
+                     (1.0f / HID);
+  float q = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float d0 = v[i].x - mean, d1 = v[i].y - mean, d2 = v[i].z - mean, d3 = v[i].w - mean;
+    q += (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+  }
+  const float rstd = 1.0f / sqrtf(block_sum(q, red) * (1.0f / HID) + eps);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  const float4* b4 = reinterpret_cast<const float4*>(b);
+  uint2* out = reinterpret_cast<uint2*>(t16 + static_cast<size_t>(row) * HID);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float4 g = __ldg(w4 + t + 128 * i);
+    float4 y = make_float4((v[i].x - mean) * rstd * g.x, (v[i].y - mean) * rstd * g.y, (v[i].z - mean) * rstd * g.z,
+                           (v[i].w - mean) * rstd * g.w);
+    if (b) {
+      const float4 c = __ldg(b4 + t + 128 * i);
+      y.x += c.x; y.y += c.y; y.z += c.z; y.w += c.w;
+    }
+    const __half2 h0 = __floats2half2_rn(y.x, y.y), h1 = __floats2half2_rn(y.z, y.w);
+    out[t + 128 * i] = make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+  }
+}
+
 inline int grid_rows(int rows) { return (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA; }
 
 }  // namespace
@@ -279,6 +366,9 @@ cudaError_t launch_embed_ln(const __half* emb, const int* tok, const float* w, f
 cudaError_t launch_ln(const float* x, const int* idx, const float* w, const float* b, float eps,
                       __half* t16, int rows, cudaStream_t s) {
   if (rows <= 0) return cudaSuccess;
+  if (rows < kSmallRows)
+    return launch_pdl(ln_row_cta_kernel<0>, dim3(rows), dim3(kRowThreads), 0, s, nullptr, 0, const_cast<float*>(x),
+                      idx, PendingParts(), w, b, eps, t16, rows);
   return launch_pdl(ln_kernel, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, idx, w, b, eps, t16,
                     static_cast<float*>(nullptr), rows);
 }
@@ -292,6 +382,9 @@ cudaError_t launch_ln_inplace(float* x, const float* w, float eps, __half* t16, 
 template <int NP>
 cudaError_t launch_ln_parts_n(float* x, const PendingParts& p, const float* w, const float* b, float eps,
                               __half* t16, int rows, cudaStream_t s) {
+  if (rows < kSmallRows)
+    return launch_pdl(ln_row_cta_kernel<NP>, dim3(rows), dim3(kRowThreads), 0, s, nullptr, 0, x,
+                      static_cast<const int*>(nullptr), p, w, b, eps, t16, rows);
   return launch_pdl(ln_parts_kernel<NP>, dim3(grid_rows(rows)), dim3(256), 0, s, nullptr, 0, x, p, w, b, eps, t16,
                     rows);
 }
