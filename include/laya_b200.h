@@ -87,7 +87,15 @@ int laya_finalize(laya_engine *e);
  * host memory, written before return.  Requests must have att in prefix form
  * (ones then zeros in every row, at least one real token), qtype < 3,
  * 0 <= mpos < l, and mpos inside the real tokens where mmask != 0 -- the
- * layout build_batch produces (src/main.rs:470-500). */
+ * layout build_batch produces (src/main.rs:470-500).
+ * The engine keeps CUDA graphs of recent request shapes (batch shape, row
+ * groups, attention work, arena generation; up to 8, least recently used
+ * out): a shape's first call launches eagerly, its second is captured on the
+ * engine's stream and later calls replay the graph, with the request uploaded
+ * anew each call.  Results are bitwise those of the eager launch.  Weight
+ * uploads and arena growth retire every graph.  One engine is not safe for
+ * concurrent calls from several threads (neither is the reference's
+ * &mut Engine).  LAYA_FORWARD_GRAPHS=0 in the environment disables the graphs. */
 int laya_forward(laya_engine *e, const laya_req *req, float *logits, float *act);
 
 /* TapSink (src/ops.rs:1-3): like laya_forward, and also calls fn with the
