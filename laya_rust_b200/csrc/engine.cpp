@@ -976,9 +976,7 @@ struct Engine {
     const int S = defer ? choose_splits(R, K) : 1;
     if (S < 2) {
       int tail_rb = 0, ts = 0;
-      // the tail split adds whole tiles and parts into different places:
-      // a bias would be added by every part, so biased GEMMs add whole tiles
-      if (defer && !bias) choose_tail(R, K, tail_rb, ts);
+      if (defer) choose_tail(R, K, tail_rb, ts);
       if (ts < 2) {
         gemm(kEpiResid, A, Wt, Out, R, H, K, r, s, nl, kind);
         return;

@@ -251,10 +251,12 @@ __device__ __forceinline__ Unit unit_of(int u, const GemmArgs& a, int num_kb) {
 // Epilogue of one warp: 32 rows (TMEM lanes) and column half `hc` of the
 // tile, i.e. columns [hc*BN/2, (hc+1)*BN/2) (for GeGLU: output columns
 // [hc*BN/4, (hc+1)*BN/4), from gate and up columns of that range).
+// `with_bias`: the f32 epilogues add a.bias (when set) -- once per output
+// element, so only by whole tiles and by K part 0 of a split tile.
 template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorMap* tmOut, Stager& st,
                                               uint32_t t_row, int row0, int row, int n0, int hc, int yoff,
-                                              bool reduce) {
+                                              bool reduce, bool with_bias) {
   const bool valid = row < a.M;
   const int r = row - row0;  // row within this warp's 32-row slab
   const int cb = hc * (BN / 2), ce = cb + BN / 2;
@@ -348,8 +350,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& a, const CUtensorM
       uint32_t v[32];
       tmem_ld_32x32b_x32(t_row + c0, v);
       tmem_ld_wait();
-      // a bias is added once: by the whole tile, or by K part 0 (yoff 0)
-      if ((EPI == kEpiResid || (EPI == kEpiPartial && yoff == 0)) && a.bias) {
+      if (with_bias && a.bias) {
         const float* b = a.bias + n0 + c0;
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] = __float_as_uint(u2f(v[j]) + __ldg(b + j));
@@ -599,12 +600,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         // stores its sums in the parts region, rows counted from tail_row0
         if (w.tail)
           epilogue_tile<EPI, BN>(args, &tmOut2, st, t_row, row0, row0 + lane, n0, hc,
-                                 w.part * args.split_rows - args.tail_row0, false);
+                                 w.part * args.split_rows - args.tail_row0, false, w.part == 0);
         else
-          epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc, 0, true);
+          epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc, 0, true, true);
       } else {
         epilogue_tile<EPI, BN>(args, &tmOut, st, t_row, row0, row0 + lane, n0, hc,
-                               EPI == kEpiPartial ? w.part * args.split_rows : 0, EPI == kEpiResid);
+                               EPI == kEpiPartial ? w.part * args.split_rows : 0, EPI == kEpiResid,
+                               EPI == kEpiResid || (EPI == kEpiPartial && w.part == 0));
       }
       tc_fence_before();
       __syncwarp();
@@ -664,10 +666,10 @@ cudaError_t launch_gemm(int epilogue, const GemmMaps& m, const GemmArgs& args, i
        args.split_rows < ((args.M + BM - 1) / BM) * BM))
     return cudaErrorInvalidValue;
   if (epilogue == kEpiResidTail) {
-    // whole row blocks before the tail, parts that fit the parts region, no
-    // bias (each part would add it)
+    // whole row blocks before the tail, parts that fit the parts region (a
+    // bias is added by whole tiles and by part 0 of the split ones)
     const int num_n = args.N / bn, num_tiles = ((args.M + BM - 1) / BM) * num_n;
-    if (bn != kGemmBN || !m.out2 || args.bias || args.splits < 1 || args.splits > args.K / BK ||
+    if (bn != kGemmBN || !m.out2 || args.splits < 1 || args.splits > args.K / BK ||
         args.main_tiles < 0 || args.main_tiles >= num_tiles || args.main_tiles % num_n ||
         args.tail_row0 != (args.main_tiles / num_n) * BM || args.split_rows % BM ||
         args.split_rows < ((args.M - args.tail_row0 + BM - 1) / BM) * BM)

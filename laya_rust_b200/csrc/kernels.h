@@ -39,7 +39,7 @@ enum GemmEpilogue : int {
   // order (deterministic), so small-M GEMMs spread their K loop over more SMs.
   kEpiPartial = 7,
   // residual GEMM whose tiles do not fill the last wave: work units below
-  // main_tiles are whole tiles reduce-added into x (kEpiResid, no bias);
+  // main_tiles are whole tiles reduce-added into x (as kEpiResid, + bias);
   // the remaining tiles (whole row blocks from tail_row0 on) are cut into
   // `splits` K parts each, and part s of a tile stores its f32 sum at rows
   // s * split_rows + (row - tail_row0) of the second output map (the parts
