@@ -22,6 +22,9 @@ Workloads (--config), all seeded synthetic data on a random-init f16 model:
                on the host threads, assigned to the GPUs greedily by token
                cost; each GPU packs its share across requests into
                <=16384-token forwards.  Steps are the forwards of one pass.
+  gemm         diagnostic: the encoder's four GEMM shapes at 9872 rows, this
+               build's kernel with its fused epilogues against cuBLAS (torch)
+               on the same shapes and operands, L2 flushed per launch.
 
   value     device-resident: requests uploaded once (plans), forwards
             enqueued back to back (CUDA graph replay where one plan repeats);
@@ -59,7 +62,7 @@ sys.path.insert(0, ROOT)
 METRIC = "encoder tokens/sec"
 UNIT = "real tokens/s"
 LAT_METRIC = "request latency p50"
-CONFIGS = ["forward-16k", "long-state", "layer", "request", "stream"]
+CONFIGS = ["forward-16k", "long-state", "layer", "request", "stream", "gemm"]
 DATA = "synthetic (seeded ids, random-init weights)"
 MODEL = "laya (ModernBERT-large 28L + 2L head), random-init f16 GGUF seed 0"
 LAYERS = (("global", 0), ("local", 1))
@@ -932,8 +935,96 @@ def stream_key(args, d, eng):
                     "e2e_value through laya_forward + scoring + response JSON (wall clock, max over ranks)"}
 
 
+# The encoder's four GEMMs at the 16384-token forward's 9872 real rows:
+# (name, N as launched, N of the layer, K, epilogue code of laya_bench_gemm,
+# f32 residual output).  Wi is launched with gate and up co-tiled and padded
+# to 21 tiles of 256 columns; its FLOPs count the layer's 2 x 2624 columns.
+GEMM_SHAPES = (("Wqkv", 3072, 3072, 1024, 0, False), ("Wo", 1024, 1024, 1024, 2, True),
+               ("Wi", 5376, 5248, 1024, 3, False), ("Wo_mlp", 1024, 1024, 2624, 2, True))
+GEMM_M = 9872
+
+
+def run_gemm(args, d):
+    """Diagnostic (not a configuration of the reference): the encoder's four
+    GEMM shapes alone, this build's tcgen05 kernel with its fused epilogue
+    (RoPE + scale, f32 residual reduce-add, GeGLU) against cuBLAS through
+    torch on the same shapes and operand values (f16 operands, f32
+    accumulation; f16 output, or for the residual shapes an f32 output that
+    adds the residual: addmm with out_dtype f32).  L2 is flushed before every
+    launch; CUDA events around each launch; rank 0 only."""
+    from laya_rust_b200 import engine as E
+    torch = d.torch
+    if d.rank != 0:
+        return
+    torch.backends.cuda.matmul.allow_fp16_reduced_precision_reduction = False
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    clocks = ClockSampler([0])
+    rows, tot_flops, tot_laya, tot_lib = [], 0.0, 0.0, 0.0
+    for name, n_launch, n, k, epi, resid in GEMM_SHAPES:
+        flops = 2.0 * GEMM_M * n * k
+        laya_ms = E.bench_gemm(GEMM_M, n_launch, k, epi, args.steps)
+        # the operand bit patterns laya_bench_gemm writes (f16 1.0039, 0.0655)
+        a = torch.full((GEMM_M, k), 0x3C3C, dtype=torch.int16, device="cuda").view(torch.float16)
+        w = torch.full((n, k), 0x2C2C, dtype=torch.int16, device="cuda").view(torch.float16)
+        x = torch.zeros((GEMM_M, n), dtype=torch.float32, device="cuda") if resid else None
+        if resid:
+            try:
+                call = lambda: torch.addmm(x, a, w.t(), out_dtype=torch.float32)
+                call()
+                lib_form = "addmm(f32 residual, f16, f16, out_dtype=f32)"
+            except RuntimeError:
+                call = lambda: torch.mm(a, w.t())
+                lib_form = "mm (f16 out; addmm with out_dtype f32 unavailable)"
+        else:
+            call = lambda: torch.mm(a, w.t())
+            lib_form = "mm (f16 out)"
+        for _ in range(max(3, args.warmup)):
+            call()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        lib_ms = sum(p.elapsed_time(q) for p, q in evs) / args.steps
+        rows.append({"gemm": name, "m": GEMM_M, "n": n, "k": k, "laya_us": laya_ms * 1e3,
+                     "laya_tflops": flops / (laya_ms / 1e3) / 1e12, "cublas_us": lib_ms * 1e3,
+                     "cublas_tflops": flops / (lib_ms / 1e3) / 1e12, "cublas_call": lib_form,
+                     "laya_over_cublas_time": laya_ms / lib_ms})
+        tot_flops += flops
+        tot_laya += laya_ms
+        tot_lib += lib_ms
+        del a, w, x
+    clk = clocks.stop()
+    pk, pk_src = peaks()
+    peak = pk["bf16_tflops"]
+    achieved = tot_flops / (tot_laya / 1e3) / 1e12
+    line = base_line(args, "encoder GEMM TFLOP/s (four shapes, fused epilogues)", achieved, "TFLOP/s", 1,
+                     tot_laya, {"workload": f"Wqkv, Wo, Wi, Wo_mlp at M = {GEMM_M} (one layer of forward-16k)",
+                                "l2": "flushed (256 MiB memset) before every launch",
+                                "operands": "constant f16 patterns, the same for both kernels"},
+                     shapes=rows,
+                     cublas={"tflops": tot_flops / (tot_lib / 1e3) / 1e12, "ms_per_layer": tot_lib,
+                             "epilogues": "none fused (plain GEMM; residual shapes add an f32 input)"},
+                     roofline={"bound": "tensor", "kernel": "gemm_tc_kernel", "achieved": achieved, "peak": peak,
+                               "unit": "TFLOP/s", "frac": achieved / peak,
+                               "peak_source": f"{pk_src} bf16_tflops (burst)", "traffic": None},
+                     gpu_launches=4 * (args.steps + 3), clocks=clk)
+    print(json.dumps(line), flush=True)
+
+
 def run_b200(args):
     d = Dist()
+    if args.config == "gemm":
+        try:
+            run_gemm(args, d)
+        finally:
+            d.close()
+        return
     eng = open_engine(d)
     try:
         if args.config in ("forward-16k", "long-state"):

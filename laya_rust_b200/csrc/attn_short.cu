@@ -99,6 +99,14 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// (x0 * inv, x1 * inv) of two f32 TMEM words in one packed multiply, as f16x2
+// (x0 in the low half); each lane rounds as the scalar multiply.
+__device__ __forceinline__ uint32_t scaled_h2(uint32_t x0, uint32_t x1, uint64_t inv2) {
+  float p, q;
+  f2_get(f2_mul(f2(u2f(x0), u2f(x1)), inv2), p, q);
+  return pack_half2(p, q);
+}
+
 // (2^x0, 2^x1) as packed f16 (x0 in the low half): the arguments are
 // rounded to f16 and one MUFU op exponentiates both.
 __device__ __forceinline__ uint32_t exp2_h2(float x0, float x1) {
@@ -130,10 +138,12 @@ __device__ __forceinline__ void chunk_max(float (&mx)[4], const uint32_t (&v)[32
   if (!any) return;
   if (all) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], u2f(v[i]));
+    for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = fmax3f(mx[(i >> 1) & 3], u2f(v[i]), u2f(v[i + 1]));
   } else {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mx[i & 3] = fmaxf(mx[i & 3], (mask >> i) & 1u ? u2f(v[i]) : -INFINITY);
+    for (int i = 0; i < 32; i += 2)
+      mx[(i >> 1) & 3] = fmax3f(mx[(i >> 1) & 3], (mask >> i) & 1u ? u2f(v[i]) : -INFINITY,
+                                (mask >> (i + 1)) & 1u ? u2f(v[i + 1]) : -INFINITY);
   }
 }
 
@@ -372,7 +382,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld_wait();
         chunk_max(mx, v, true, all[ch], mask[ch]);
       }
-      const float m = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      const float m = fmax3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
       const float ms = (m == -INFINITY ? 0.0f : m) * L2E;
 #pragma unroll
       for (int ch = 0; ch < 4; ++ch) {
@@ -402,20 +412,19 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_free[s]);
       if (r < tile.y) {
-        const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+        const uint64_t inv2 = f2_splat(sum > 0.0f ? 1.0f / sum : 0.0f);
         uint4* dst = reinterpret_cast<uint4*>(a.out + static_cast<size_t>(tile.x + r) * 1024 + h * D);
 #pragma unroll
         for (int x = 0; x < 4; ++x)
-          dst[x] = make_uint4(pack_half2(u2f(o0[8 * x]) * inv, u2f(o0[8 * x + 1]) * inv),
-                              pack_half2(u2f(o0[8 * x + 2]) * inv, u2f(o0[8 * x + 3]) * inv),
-                              pack_half2(u2f(o0[8 * x + 4]) * inv, u2f(o0[8 * x + 5]) * inv),
-                              pack_half2(u2f(o0[8 * x + 6]) * inv, u2f(o0[8 * x + 7]) * inv));
+          dst[x] = make_uint4(scaled_h2(o0[8 * x], o0[8 * x + 1], inv2), scaled_h2(o0[8 * x + 2], o0[8 * x + 3], inv2),
+                              scaled_h2(o0[8 * x + 4], o0[8 * x + 5], inv2),
+                              scaled_h2(o0[8 * x + 6], o0[8 * x + 7], inv2));
 #pragma unroll
         for (int x = 0; x < 4; ++x)
-          dst[4 + x] = make_uint4(pack_half2(u2f(o1[8 * x]) * inv, u2f(o1[8 * x + 1]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 2]) * inv, u2f(o1[8 * x + 3]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 4]) * inv, u2f(o1[8 * x + 5]) * inv),
-                                  pack_half2(u2f(o1[8 * x + 6]) * inv, u2f(o1[8 * x + 7]) * inv));
+          dst[4 + x] = make_uint4(scaled_h2(o1[8 * x], o1[8 * x + 1], inv2),
+                                  scaled_h2(o1[8 * x + 2], o1[8 * x + 3], inv2),
+                                  scaled_h2(o1[8 * x + 4], o1[8 * x + 5], inv2),
+                                  scaled_h2(o1[8 * x + 6], o1[8 * x + 7], inv2));
       }
       tile = tile_n;
       lo = hi = 0;

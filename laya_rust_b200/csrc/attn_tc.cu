@@ -535,13 +535,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           tmem_ld_wait();
           if (ch ? all1 : all0) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], u2f(v[j]));
+            for (int j = 0; j < 32; j += 2) mx[(j >> 1) & 3] = fmax3f(mx[(j >> 1) & 3], u2f(v[j]), u2f(v[j + 1]));
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], (mask >> j) & 1u ? u2f(v[j]) : -INFINITY);
+            for (int j = 0; j < 32; j += 2)
+              mx[(j >> 1) & 3] = fmax3f(mx[(j >> 1) & 3], (mask >> j) & 1u ? u2f(v[j]) : -INFINITY,
+                                        (mask >> (j + 1)) & 1u ? u2f(v[j + 1]) : -INFINITY);
           }
         }
-        const float mh = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+        const float mh = fmax3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
         // the row's block maximum: this half's and the other half's
         xmax_s[(par * 2 + half) * TQ + row] = mh;
         named_sync(bar_id, 64);

@@ -306,6 +306,13 @@ __device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
 }
 __device__ __forceinline__ uint64_t f2_splat(float v) { return f2(v, v); }
 
+// max(a, b, c) as one sm_100 three-input max (the same value as two fmaxf).
+__device__ __forceinline__ float fmax3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // (gelu_erf(v0), gelu_erf(v1)) in packed pairs: the same A&S 7.1.26 formula,
 // with the polynomial's coefficients negated so that erf(|x|) = 1 + p e is
 // one fused step.  The divide and the exponential stay per lane (MUFU).

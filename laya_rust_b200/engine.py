@@ -83,6 +83,7 @@ def lib():
                                          ctypes.c_int, ctypes.c_int]
         L.laya_selftest_attention.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_int32),
                                               ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+        L.laya_bench_gemm.argtypes = [ctypes.c_int] * 8 + [_f32p]
         _lib = L
     return _lib
 
@@ -295,6 +296,16 @@ def selftest_gemm(a: np.ndarray, w: np.ndarray, device: int = 0, tile_n: int = 2
     _check(lib().laya_selftest_gemm(device, a.ctypes.data, w.ctypes.data, out.ctypes.data_as(_f32p), m, n, k,
                                     tile_n))
     return out
+
+
+def bench_gemm(m: int, n: int, k: int, epi: int, iters: int, device: int = 0, tile_n: int = 256,
+               flush_l2: bool = True) -> float:
+    """Mean device time (ms) of one launch of the tcgen05 GEMM with the
+    forward's epilogue `epi` on [m, k] x [n, k]^T (operands of a fixed
+    pattern; with flush_l2 a 256 MiB memset runs untimed before each launch)."""
+    ms = ctypes.c_float(0.0)
+    _check(lib().laya_bench_gemm(device, m, n, k, tile_n, epi, 1 if flush_l2 else 0, iters, ctypes.byref(ms)))
+    return float(ms.value)
 
 
 def selftest_attention(qkv: np.ndarray, lens, window: int, device: int = 0, impl: int = 1) -> np.ndarray:
