@@ -690,7 +690,7 @@ struct Engine {
           for (size_t i = 0; i < el; ++i) h[i] = f2h_or_copy(data, is_f16, i);
         }
         wt.buf.alloc(h.size() * 2, "weight alloc");
-        ck(cudaMemcpy(wt.buf.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+        upload_sync(wt.buf.p, h.data(), h.size() * 2, "weight upload");
         if (role.kind == Kind::Linear) {
           const uint64_t rows = wi ? (uint64_t)2 * INTER_PAD : (uint64_t)role.shape[0];
           const uint64_t kdim = (uint64_t)role.shape[1];
@@ -707,7 +707,7 @@ struct Engine {
         std::vector<float> f(el);
         for (size_t i = 0; i < el; ++i) f[i] = f32_at(i);
         wt.buf.alloc(el * 4, "weight alloc");
-        ck(cudaMemcpy(wt.buf.p, f.data(), el * 4, cudaMemcpyHostToDevice), "weight upload");
+        upload_sync(wt.buf.p, f.data(), el * 4, "weight upload");
         if (role.kind == Kind::Rope || name == "scorer.3.bias") wt.host = f;
         break;
       }
@@ -753,6 +753,16 @@ struct Engine {
   }
 
   // graph.rs:62-84: cos/sin(p * freq[j]) in f32 with libm cosf/sinf.
+  // Host -> device copy on the engine's stream, complete on return.  The
+  // engine's streams are non-blocking: a cudaMemcpy or cudaMemset on the
+  // legacy default stream is not ordered before their kernels (and from
+  // pageable memory may return before its DMA lands), so every write into the
+  // engine's buffers goes through its own stream.
+  void upload_sync(void* dst, const void* src, size_t bytes, const char* what) {
+    ck(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream), what);
+    ck(cudaStreamSynchronize(stream), what);
+  }
+
   void ensure_rope(int len) {
     if (len <= rope_len) return;
     int n = rope_len ? rope_len : 512;
@@ -773,10 +783,10 @@ struct Engine {
     // the tables move: graphs captured over the old ones must not replay
     ++arena_gen;
     for (auto* pr : {&cos_full, &sin_full, &cos_slide, &sin_slide}) pr->alloc((size_t)n * 32 * 4, "rope alloc");
-    ck(cudaMemcpy(cos_full.p, cf.data(), cf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    ck(cudaMemcpy(sin_full.p, sf.data(), sf.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    ck(cudaMemcpy(cos_slide.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope upload");
-    ck(cudaMemcpy(sin_slide.p, ss.data(), ss.size() * 4, cudaMemcpyHostToDevice), "rope upload");
+    upload_sync(cos_full.p, cf.data(), cf.size() * 4, "rope upload");
+    upload_sync(sin_full.p, sf.data(), sf.size() * 4, "rope upload");
+    upload_sync(cos_slide.p, cs.data(), cs.size() * 4, "rope upload");
+    upload_sync(sin_slide.p, ss.data(), ss.size() * 4, "rope upload");
     rope_len = n;
   }
 
@@ -803,8 +813,9 @@ struct Engine {
     partial.alloc((size_t)kScorerPartials * cap_mk * 4, "arena partial");
     out_logits.alloc((size_t)cap_mk * 4, "arena logits");
     out_act.alloc((size_t)cap_n * 2 * 4, "arena act");
+    // on the engine's stream, so the clears precede the forward's kernels
     for (DevBuf* b : {&x, &t16, &qkv, &ctx, &gate, &hmlp, &mk16, &partial})
-      ck(cudaMemset(b->p, 0, b->bytes), "arena clear");
+      ck(cudaMemsetAsync(b->p, 0, b->bytes, stream), "arena clear");
   }
 
   // The split-K part regions: allocated once, with a plan (never while a
@@ -1493,7 +1504,8 @@ Engine* open_engine(int device) {
   ck(cudaEventCreateWithFlags(&e->ev_fork, cudaEventDisableTiming), "event create");
   ck(cudaEventCreateWithFlags(&e->ev_join, cudaEventDisableTiming), "event create");
   e->err.alloc(256, "error word");
-  ck(cudaMemset(e->err.p, 0, 256), "error word clear");
+  ck(cudaMemsetAsync(e->err.p, 0, 256, e->stream), "error word clear");
+  ck(cudaStreamSynchronize(e->stream), "sync");
   return e.release();
 }
 

@@ -3,7 +3,8 @@ launched eagerly the first time, captured on its second call and replayed
 after that.  A replay reads the request through the same device buffer, so
 it must give bitwise the eager forward's logits and act -- for the request it
 was captured on and for any other request of the same shape -- and a weight
-uploaded again must retire the graph (it holds the old weight pointers)."""
+uploaded again must retire the graph (it holds the old weight pointers).
+Two engines given the same requests agree bit for bit."""
 import numpy as np
 import pytest
 
@@ -78,3 +79,22 @@ def test_a_longer_request_retires_the_graphs():
             assert same(eng.forward(short), eager(eng, short))
     finally:
         eng.close()
+
+
+def test_two_engines_agree_bitwise_through_arena_growth():
+    """A forward that grows the arena clears the new buffers on the engine's
+    own stream before its kernels run (a clear on the legacy default stream
+    is not ordered before a non-blocking stream's kernels).  Two fresh
+    engines fed the same requests of growing size -- every one of them grows
+    the arena -- must agree bit for bit on each."""
+    reqs = [synthetic_req(91, [94, 85], 2), synthetic_req(92, [371], 2), synthetic_req(93, [146] * 5, 5),
+            synthetic_req(94, [300] * 6, 4), synthetic_req(95, [120] * 40, 3)]
+    outs = []
+    for _ in range(2):
+        e = E.Engine(modelgen.cached_model(seed=0), device=0)
+        try:
+            outs.append([e.forward(r) for r in reqs])
+        finally:
+            e.close()
+    for i, (a, b) in enumerate(zip(*outs)):
+        assert same(a, b), f"request {i}"
