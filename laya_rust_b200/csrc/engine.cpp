@@ -664,6 +664,10 @@ struct Engine {
     // (a plan's graph records the arena generation and is re-captured)
     tail_cache_ready = false;
     ++arena_gen;
+    // work already queued on the engine's streams (a plan run) may still
+    // read the buffer this upload replaces
+    ck(cudaStreamSynchronize(stream), "sync");
+    if (side) ck(cudaStreamSynchronize(side), "sync");
     Weight& wt = w[name];
     switch (role.kind) {
       case Kind::Linear:
