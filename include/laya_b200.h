@@ -65,7 +65,9 @@ int laya_open_empty(int device, laya_engine **out);
 
 /* Uploads one tensor named as in src/arch.rs, in STORED layout (the GGUF /
  * PyTorch [out, in] layout, dims as Tensors::stored_dims reports them,
- * src/weights.rs:261-268) -- not the transposed graph layout. */
+ * src/weights.rs:261-268) -- not the transposed graph layout.  The copy is
+ * complete on return; an upload that replaces a tensor first waits for the
+ * engine's queued work (plan runs) that may still read the old one. */
 int laya_upload_weight_f16(laya_engine *e, const char *name, const uint16_t *data,
                            const int64_t *stored_dims, int ndims);
 int laya_upload_weight_f32(laya_engine *e, const char *name, const float *data,
