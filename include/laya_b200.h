@@ -132,7 +132,10 @@ int laya_plan_stats(laya_plan *p, int64_t *real_tokens, int64_t *launches, int64
 #define LAYA_PROF_KINDS 8
 int laya_plan_profile(laya_engine *e, laya_plan *p, int steps, double *ms, int64_t *launches);
 void laya_plan_destroy(laya_plan *p);
-/* The cudaStream_t the engine launches on. */
+/* The cudaStream_t the engine launches on.  It is a non-blocking stream: work
+ * the host issues on the legacy default stream (cudaMemcpy, cudaMemset, NULL-
+ * stream launches) is not ordered with it, so a host that feeds or reads the
+ * engine's buffers does so on this stream or synchronizes both. */
 void *laya_stream(laya_engine *e);
 /* One encoder layer in isolation (a benchmark configuration, the body of the
  * layer loop of graph.rs:103-123): set the residual stream of the plan's real
