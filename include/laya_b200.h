@@ -132,6 +132,18 @@ int laya_plan_stats(laya_plan *p, int64_t *real_tokens, int64_t *launches, int64
 #define LAYA_PROF_KINDS 8
 int laya_plan_profile(laya_engine *e, laya_plan *p, int steps, double *ms, int64_t *launches);
 void laya_plan_destroy(laya_plan *p);
+/* The host side of a request's plan, with no device or engine (tests and
+ * diagnostics): the validation laya_forward applies, with the same errors,
+ * then the work the forward would launch.  *rows: the real tokens, compacted
+ * sequence after sequence.  Tiles (2 ints each): (first row, rows) of the
+ * attention tiles that pack consecutive sequences of at most 128 tokens.
+ * Items (4 ints each): (first query row, query rows, sequence's first row,
+ * sequence length) of the flash work items, one per 128 query rows of each
+ * longer sequence, longest sequences first.  Counts are always written;
+ * `tiles` / `items` may be NULL, else must hold cap_tiles / cap_items
+ * entries (fewer than needed: LAYA_E_INVALID). */
+int laya_plan_layout(const laya_req *req, int64_t *rows, int64_t *ntiles, int32_t *tiles, int64_t cap_tiles,
+                     int64_t *nitems, int32_t *items, int64_t cap_items);
 /* The cudaStream_t the engine launches on.  It is a non-blocking stream: work
  * the host issues on the legacy default stream (cudaMemcpy, cudaMemset, NULL-
  * stream launches) is not ordered with it, so a host that feeds or reads the

@@ -1727,6 +1727,33 @@ int laya_plan_profile(laya_engine* e, laya_plan* p, int steps, double* ms, int64
 
 void laya_plan_destroy(laya_plan* p) { delete p; }
 
+int laya_plan_layout(const laya_req* req, int64_t* rows, int64_t* ntiles, int32_t* tiles, int64_t cap_tiles,
+                     int64_t* nitems, int32_t* items, int64_t cap_items) {
+  return guard([&] {
+    if (!rows || !ntiles || !nitems) throw Error(LAYA_E_INVALID, "null argument");
+    const laya::HostPlan p = laya::make_plan(req);
+    *rows = p.R;
+    *ntiles = p.ntiles;
+    *nitems = p.nitems;
+    if (tiles) {
+      if (cap_tiles < p.ntiles) throw Error(LAYA_E_INVALID, "tile capacity too small");
+      for (int i = 0; i < p.ntiles; ++i) {
+        tiles[2 * i] = p.tiles[i].x;
+        tiles[2 * i + 1] = p.tiles[i].y;
+      }
+    }
+    if (items) {
+      if (cap_items < p.nitems) throw Error(LAYA_E_INVALID, "item capacity too small");
+      for (int i = 0; i < p.nitems; ++i) {
+        items[4 * i] = p.items[i].x;
+        items[4 * i + 1] = p.items[i].y;
+        items[4 * i + 2] = p.items[i].z;
+        items[4 * i + 3] = p.items[i].w;
+      }
+    }
+  });
+}
+
 void* laya_stream(laya_engine* e) { return e ? (void*)e->e->stream : nullptr; }
 
 int laya_plan_set_hidden(laya_engine* e, laya_plan* p, const float* x) {

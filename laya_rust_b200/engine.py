@@ -84,6 +84,9 @@ def lib():
         L.laya_selftest_attention.argtypes = [ctypes.c_int, vp, ctypes.POINTER(ctypes.c_int32),
                                               ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
         L.laya_bench_gemm.argtypes = [ctypes.c_int] * 8 + [_f32p]
+        _i32p = ctypes.POINTER(ctypes.c_int32)
+        L.laya_plan_layout.argtypes = [ctypes.POINTER(_CReq), _i64p, _i64p, _i32p, ctypes.c_int64, _i64p, _i32p,
+                                       ctypes.c_int64]
         _lib = L
     return _lib
 
@@ -296,6 +299,23 @@ def selftest_gemm(a: np.ndarray, w: np.ndarray, device: int = 0, tile_n: int = 2
     _check(lib().laya_selftest_gemm(device, a.ctypes.data, w.ctypes.data, out.ctypes.data_as(_f32p), m, n, k,
                                     tile_n))
     return out
+
+
+def plan_layout(req: Req) -> tuple[int, np.ndarray, np.ndarray]:
+    """laya_plan_layout: (real rows, tiles [T, 2], items [I, 4]) of the
+    request's host plan, with no device; raises LayaError as laya_forward
+    would for an invalid request."""
+    c = req._c()
+    rows, nt, ni = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_int64()
+    L = lib()
+    _check(L.laya_plan_layout(ctypes.byref(c), ctypes.byref(rows), ctypes.byref(nt), None, 0, ctypes.byref(ni),
+                              None, 0))
+    tiles = np.zeros((nt.value, 2), np.int32)
+    items = np.zeros((ni.value, 4), np.int32)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    _check(L.laya_plan_layout(ctypes.byref(c), ctypes.byref(rows), ctypes.byref(nt), tiles.ctypes.data_as(i32p),
+                              nt.value, ctypes.byref(ni), items.ctypes.data_as(i32p), ni.value))
+    return rows.value, tiles, items
 
 
 def bench_gemm(m: int, n: int, k: int, epi: int, iters: int, device: int = 0, tile_n: int = 256,
